@@ -1,0 +1,375 @@
+"""LLMEngine: the Python shell over the native core.
+
+Each ``step()``: the C++ scheduler picks the batch (continuous batching,
+chunked prefill, preemption) -> the executor runs the forward on every
+tensor-parallel rank -> the fused GPU sampler draws tokens -> the C++ core
+appends them and applies stop rules -> Python builds outputs only for
+requests that stream, need stop strings or logprobs, or just finished.
+
+Parity: python/swiftllm/engine.py:107-392 (LLMEngine add_request /
+abort_request / step / has_unfinished_requests) and the Rust Engine
+(crates/swiftllm-core/src/engine.rs: add_request :123-135, abort_request
+:149-153, step :161-199, stats :259-267). The reference's step only
+schedules and bumps a counter (engine.rs:188-198); this one runs the model.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional
+
+import numpy as np
+
+from .. import _core
+from ..config import EngineConfig, LoRARequest, PreemptionMode, SamplingParams, SchedulerPolicy
+from ..outputs import CompletionOutput, FinishReason, RequestOutput, TokenLogprob
+from ..utils.logging import get_logger
+from ..utils import nvtx
+
+log = get_logger(__name__)
+
+
+@dataclass
+class _Req:
+    request_id: str
+    prompt: Optional[str]
+    prompt_ids: List[int]
+    params: SamplingParams
+    gid: int
+    stream: bool = False
+    texts: Dict[int, str] = field(default_factory=dict)       # seq -> text so far
+    stop_reason: Dict[int, Any] = field(default_factory=dict)
+    logprobs: Dict[int, List[TokenLogprob]] = field(default_factory=dict)
+    finished_seqs: Dict[int, str] = field(default_factory=dict)
+    done: bool = False
+
+
+class LLMEngine:
+    def __init__(self, config: EngineConfig):
+        self.config = config
+        self._initialized = False
+        self._reqs: Dict[str, _Req] = {}
+        self._by_gid: Dict[int, _Req] = {}
+        self._counter = 0
+        self.tokenizer = None
+        self.model_config = None
+        self.executor = None
+        self.scheduler = None
+        self.block_manager = None
+        self.sampler = None
+        self.spec = None
+        self._t_start = time.monotonic()
+        self._gen_tokens = 0
+        self._prompt_tokens = 0
+        self._aborted: List[str] = []
+
+    # ------------------------------------------------------------ init
+    def _ensure_initialized(self) -> None:
+        if self._initialized:
+            return
+        from ..model_resolver import resolve_model
+        from ..models.config import load_config
+        from .tokenizer import load_tokenizer
+        from ..parallel.executor import make_executor
+        from ..sampling.batch import BatchSampler
+        c = self.config
+        path = c.model
+        if c.load_format != "dummy":
+            path = resolve_model(c.model, download_dir=c.download_dir)
+            c.model = path
+        self.model_config = load_config(path)
+        mcfg = self.model_config
+        max_len = c.max_model_len or min(mcfg.max_position_embeddings, 4096)
+        c.max_model_len = max_len
+        if c.max_num_batched_tokens is None:
+            c.max_num_batched_tokens = max(max_len, 8192) if not c.enable_chunked_prefill \
+                else max(c.max_prefill_tokens, 2048)
+        if not c.enable_chunked_prefill and c.max_num_batched_tokens < max_len:
+            c.max_num_batched_tokens = max_len
+        tok_path = c.tokenizer if c.tokenizer and c.tokenizer != "" else path
+        self.tokenizer = load_tokenizer(tok_path, mcfg.vocab_size, c.trust_remote_code)
+        self.eos_token_id = getattr(self.tokenizer, "eos_token_id", None)
+        if self.eos_token_id is None:
+            self.eos_token_id = mcfg.eos_token_id
+        self.executor = make_executor(mcfg, c)
+        num_gpu, num_cpu = self.executor.num_gpu_blocks, self.executor.num_cpu_blocks
+        self.block_manager = _core.BlockManager(c.block_size, num_gpu, num_cpu, c.watermark,
+                                                c.enable_prefix_caching)
+        sc = _core.SchedulerConfig()
+        sc.max_num_seqs = c.max_num_seqs
+        sc.max_num_batched_tokens = int(c.max_num_batched_tokens)
+        sc.max_model_len = int(max_len)
+        sc.enable_chunked_prefill = bool(c.enable_chunked_prefill)
+        sc.policy = {SchedulerPolicy.FCFS: _core.Policy.FCFS, SchedulerPolicy.SJF: _core.Policy.SJF,
+                     SchedulerPolicy.PRIORITY: _core.Policy.PRIORITY}[c.scheduler_policy]
+        sc.preemption = (_core.Preempt.SWAP if c.preemption_mode == PreemptionMode.SWAP and num_cpu > 0
+                         else _core.Preempt.RECOMPUTE)
+        self.scheduler = _core.Scheduler(sc, self.block_manager)
+        self.sampler = BatchSampler(mcfg.vocab_size, c.seed, self.executor.device)
+        if c.speculative_model:
+            from .speculative import SpeculativeDecoder
+            self.spec = SpeculativeDecoder(self, c.speculative_model, c.num_speculative_tokens)
+        self._initialized = True
+        log.info("engine ready: %s, %d GPU blocks, %d CPU blocks, tp=%d", mcfg.name or path,
+                 num_gpu, num_cpu, c.tensor_parallel_size)
+
+    # ------------------------------------------------------------ requests
+    def add_request(self, request_id: str, prompt: Optional[str] = None,
+                    sampling_params: Optional[SamplingParams] = None,
+                    prompt_token_ids: Optional[List[int]] = None,
+                    lora_request: Optional[LoRARequest] = None,
+                    arrival_time: Optional[float] = None, priority: int = 0,
+                    stream: bool = False) -> None:
+        self._ensure_initialized()
+        if request_id in self._reqs:
+            raise ValueError(f"duplicate request id {request_id!r}")
+        sp = sampling_params or SamplingParams()
+        if prompt_token_ids is None:
+            if prompt is None:
+                raise ValueError("either prompt or prompt_token_ids is required")
+            prompt_token_ids = list(self.tokenizer.encode(prompt))
+        if sp.use_beam_search:
+            raise NotImplementedError("beam search is not supported; use n/best_of sampling")
+        gp = _core.GroupParams()
+        gp.n = max(sp.n, sp.best_of)
+        gp.max_tokens = sp.max_tokens
+        gp.min_tokens = sp.min_tokens
+        gp.ignore_eos = sp.ignore_eos
+        gp.eos_token_id = int(self.eos_token_id) if self.eos_token_id is not None else -1
+        gp.stop_token_ids = list(sp.stop_token_ids or [])
+        gp.temperature = sp.temperature
+        gp.top_p = sp.top_p
+        gp.top_k = sp.top_k
+        gp.min_p = sp.min_p
+        gp.presence_penalty = sp.presence_penalty
+        gp.frequency_penalty = sp.frequency_penalty
+        gp.repetition_penalty = sp.repetition_penalty
+        gp.seed = -1 if sp.seed is None else int(sp.seed)
+        gp.priority = priority
+        arrival = time.monotonic() if arrival_time is None else arrival_time
+        ids = np.asarray(prompt_token_ids, dtype=np.int32)
+        if ids.size and (ids.min() < 0 or ids.max() >= self.model_config.vocab_size):
+            raise ValueError("prompt token id out of vocabulary range")
+        gid = self.scheduler.add_request(request_id, ids, gp, arrival)
+        r = _Req(request_id, prompt, list(map(int, prompt_token_ids)), sp, gid, stream=stream)
+        self._reqs[request_id] = r
+        self._by_gid[gid] = r
+        self._prompt_tokens += len(prompt_token_ids)
+
+    def abort_request(self, request_id) -> None:
+        ids = [request_id] if isinstance(request_id, str) else list(request_id)
+        for rid in ids:
+            r = self._reqs.get(rid)
+            if r is None:
+                continue
+            self.scheduler.abort_request(rid)
+            self._aborted.append(rid)
+
+    def get_num_unfinished_requests(self) -> int:
+        return len([r for r in self._reqs.values() if not r.done])
+
+    def has_unfinished_requests(self) -> bool:
+        return self.get_num_unfinished_requests() > 0
+
+    # ------------------------------------------------------------ step
+    def _history(self, sid: int):
+        prompt = self.scheduler.seq_tokens(sid, False)
+        info = self.scheduler.seq_info(sid)
+        n = info["num_prompt"]
+        return prompt[:n], prompt[n:]
+
+    def step(self) -> List[RequestOutput]:
+        self._ensure_initialized()
+        outs: List[RequestOutput] = []
+        for rid in self._aborted:
+            r = self._reqs.get(rid)
+            if r is not None and not r.done:
+                outs.append(self._final_output(r, aborted=True))
+        self._aborted = []
+        if self.spec is not None:
+            return outs + self.spec.step()
+        with nvtx.range("schedule"):
+            b = self.scheduler.schedule(time.monotonic())
+        for g in b.preempted_groups:
+            if g < 0:  # rejected: prompt can never fit the KV pool
+                r = self._by_gid.get(-g)
+                if r is not None:
+                    log.warning("request %s rejected: prompt exceeds KV cache capacity", r.request_id)
+                    outs.append(self._final_output(r))
+        if b.num_seqs == 0 and b.swap_in.size == 0 and b.swap_out.size == 0:
+            return outs
+        from ..runtime.model_runner import step_input_from_batch
+        si = step_input_from_batch(b)
+        logits = self.executor.execute(si)
+        if b.num_sample_rows == 0:
+            return outs
+        with nvtx.range("sample"):
+            toks, lps = self.sampler(logits, b, self._history)
+        want_lp = None
+        if any(self._by_gid[g].params.logprobs for g in set(np.asarray(b.sample_group).tolist())
+               if g in self._by_gid):
+            want_lp = self._top_logprobs(logits, b, toks)
+        res = self.scheduler.update(b, toks, lps, time.monotonic())
+        self._gen_tokens += len(res.token)
+        return outs + self._process(res, want_lp)
+
+    def _top_logprobs(self, logits, b, toks):
+        import torch
+        lidx = torch.from_numpy(np.asarray(b.sample_logit_idx, dtype=np.int64)).to(logits.device)
+        groups = np.asarray(b.sample_group)
+        n = max((self._by_gid[g].params.logprobs or 0) for g in groups if g in self._by_gid)
+        lp = torch.log_softmax(logits.index_select(0, lidx).float(), dim=-1)
+        top_v, top_i = lp.topk(max(n, 1), dim=-1)
+        chosen = lp.gather(1, torch.from_numpy(toks.astype(np.int64)).to(lp.device).view(-1, 1))
+        return top_v.cpu().numpy(), top_i.cpu().numpy(), chosen.view(-1).cpu().numpy()
+
+    def _decode(self, ids) -> str:
+        return self.tokenizer.decode(list(map(int, ids)), skip_special_tokens=True)
+
+    def _process(self, res, want_lp) -> List[RequestOutput]:
+        outs: List[RequestOutput] = []
+        groups = res.group
+        seqs = res.seq
+        toks = res.token
+        rows = res.row
+        touched = set()
+        for j in range(len(groups)):
+            r = self._by_gid.get(int(groups[j]))
+            if r is None:
+                continue
+            sp = r.params
+            if not (sp.stop or r.stream or sp.logprobs is not None):
+                continue
+            sid = int(seqs[j])
+            if sp.logprobs is not None and want_lp is not None:
+                tv, ti, ch = want_lp
+                row = int(rows[j])
+                lst = r.logprobs.setdefault(sid, [])
+                lst.append(TokenLogprob(int(toks[j]), self._decode([toks[j]]), float(ch[row]),
+                                        bytes=None))
+                top = r.__dict__.setdefault("top_logprobs", {}).setdefault(sid, [])
+                top.append({int(ti[row, q]): float(tv[row, q]) for q in range(sp.logprobs)})
+            if sp.stop:
+                text = self._decode(self.scheduler.seq_tokens(sid, True))
+                for s in sp.stop:
+                    k = text.find(s)
+                    if k >= 0:
+                        r.texts[sid] = text[:k + len(s)] if sp.include_stop_str_in_output else text[:k]
+                        r.stop_reason[sid] = s
+                        self.scheduler.finish_seq(sid, "stop")
+                        break
+            touched.add(r.request_id)
+        finished = set(int(g) for g in res.finished_groups)
+        # groups finished by stop strings (finish_seq) are not in finished_groups
+        for rid in list(touched):
+            r = self._reqs[rid]
+            if r.gid in finished:
+                continue
+            info = self.scheduler.group_info(r.gid)
+            if info is not None and all(self.scheduler.seq_info(s)["status"] not in
+                                        ("running", "waiting", "swapped") for s in info["seqs"]):
+                finished.add(r.gid)
+        for gid in finished:
+            r = self._by_gid.get(gid)
+            if r is not None and not r.done:
+                outs.append(self._final_output(r))
+                touched.discard(r.request_id)
+        for rid in touched:
+            r = self._reqs.get(rid)
+            if r is not None and r.stream and not r.done:
+                outs.append(self._make_output(r, final=False))
+        return outs
+
+    def _make_output(self, r: _Req, final: bool, aborted: bool = False) -> RequestOutput:
+        info = self.scheduler.group_info(r.gid)
+        comps: List[CompletionOutput] = []
+        seq_ids = info["seqs"] if info else []
+        for idx, sid in enumerate(seq_ids):
+            si = self.scheduler.seq_info(sid)
+            ids = self.scheduler.seq_tokens(sid, True).tolist()
+            text = r.texts.get(sid)
+            if text is None:
+                text = self._decode(ids)
+            status = si["status"]
+            fr = None
+            if aborted or status == "abort":
+                fr = FinishReason.ABORT
+            elif status == "stop":
+                fr = FinishReason.STOP
+            elif status == "length":
+                fr = FinishReason.LENGTH
+            stop_reason = r.stop_reason.get(sid)
+            if fr == FinishReason.STOP and stop_reason is None and ids:
+                stop_reason = ids[-1] if ids[-1] != self.eos_token_id else None
+            comps.append(CompletionOutput(
+                index=idx, text=text, token_ids=ids,
+                cumulative_logprob=float(si["cum_logprob"]),
+                logprobs=r.logprobs.get(sid), finish_reason=fr if final or fr else None,
+                stop_reason=stop_reason))
+        if final and r.params.best_of > r.params.n and len(comps) > r.params.n:
+            comps.sort(key=lambda c: -(c.cumulative_logprob or 0.0))
+            comps = comps[: r.params.n]
+            for i, c in enumerate(comps):
+                c.index = i
+        metrics = None
+        if info:
+            arr, ft, fin = info["arrival"], info["first_token"], info["finished"]
+            if fin < 0 and final:
+                fin = time.monotonic()
+            n_out = max((len(c.token_ids) for c in comps), default=0)
+            metrics = {
+                "arrival_time": arr, "first_scheduled_time": info["first_scheduled"],
+                "first_token_time": ft, "finished_time": fin if final else -1.0,
+                "ttft": (ft - arr) if ft >= 0 else None,
+                "tpot": ((fin - ft) / (n_out - 1)) if final and ft >= 0 and n_out > 1 else None,
+                "prompt_tokens": len(r.prompt_ids), "completion_tokens": sum(len(c.token_ids) for c in comps),
+                "num_preemptions": info["num_preemptions"],
+            }
+        return RequestOutput(request_id=r.request_id, prompt=r.prompt, prompt_token_ids=r.prompt_ids,
+                             outputs=comps, finished=final, metrics=metrics)
+
+    def _final_output(self, r: _Req, aborted: bool = False) -> RequestOutput:
+        out = self._make_output(r, final=True, aborted=aborted)
+        r.done = True
+        self.scheduler.release_group(r.gid)
+        self._reqs.pop(r.request_id, None)
+        self._by_gid.pop(r.gid, None)
+        return out
+
+    # ------------------------------------------------------------ stats
+    def stats(self) -> Dict[str, Any]:
+        self._ensure_initialized()
+        st = self.scheduler.stats()
+        bm = self.block_manager
+        el = max(time.monotonic() - self._t_start, 1e-9)
+        return {
+            "num_running": self.scheduler.num_running,
+            "num_waiting": self.scheduler.num_waiting,
+            "num_swapped": self.scheduler.num_swapped,
+            "completed_requests": st.finished,
+            "aborted_requests": st.aborted,
+            "throughput_tps": self._gen_tokens / el,
+            "gpu_block_utilization": 1.0 - bm.num_free_gpu_blocks / max(bm.num_gpu_blocks, 1),
+            "cpu_block_utilization": (1.0 - bm.num_free_cpu_blocks / bm.num_cpu_blocks)
+            if bm.num_cpu_blocks else 0.0,
+            "free_gpu_blocks": bm.num_free_gpu_blocks,
+            "free_cpu_blocks": bm.num_free_cpu_blocks,
+            "prefill_tokens": st.prefill_tokens,
+            "decode_tokens": st.decode_tokens,
+            "forward_passes": st.steps,
+            "num_preemptions": st.num_preemptions,
+            "prefix_cache_hit_rate": (st.prefix_cache_hit_tokens / st.prefix_cache_query_tokens)
+            if st.prefix_cache_query_tokens else 0.0,
+        }
+
+    def shutdown(self) -> None:
+        if self.executor is not None:
+            self.executor.shutdown()
+            self.executor = None
+
+    def __del__(self):
+        try:
+            self.shutdown()
+        except Exception:
+            pass

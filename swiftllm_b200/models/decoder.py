@@ -1,0 +1,297 @@
+"""Decoder-only transformer covering the Llama family (Llama 2/3, Mistral,
+Qwen2 with qkv bias), Mixtral (MoE) and Phi (LayerNorm, GELU, partial
+rotary, parallel attention/MLP block).
+
+Parity: crates/swiftllm-models/src/architectures/{llama.rs, mistral.rs,
+qwen.rs, phi.rs} (structure only in the reference: its forward returns zeros)
+and crates/swiftllm-models/src/layers/* (QKVProjection :152-192,
+GateUpProjection :194-224, FusedGatedMlp mlp.rs:169-205, MoeMlp
+mlp.rs:207-258, FusedAddRMSNorm normalization.rs:153-180).
+
+Layout (one process per GPU, tensor parallel over ``tp.size`` ranks):
+  wqkv   [(Hq + 2 Hkv) D / tp, H]  column-parallel, q heads then k then v
+  wo     [H, Hq D / tp]            row-parallel -> reduction across ranks
+  w13    [2 I / tp, H]             gate rows then up rows (per rank)
+  w2     [H, I / tp]               row-parallel -> reduction across ranks
+  MoE    router [E, H] (replicated), w13 [E, 2 I / tp, H], w2 [E, H, I / tp]
+The residual stream is replicated on every rank; the reduction after each
+row-parallel GEMM is the fused GEMM + NVLink reduce (``tp.reduce``), or
+NCCL all-reduce in the baseline backend.
+"""
+
+from __future__ import annotations
+
+import math
+import zlib
+from dataclasses import dataclass
+from types import SimpleNamespace
+from typing import Callable, Dict, List, Optional
+
+import torch
+
+from .. import ops
+from .config import ModelConfig
+from .rope import cos_sin_table
+
+
+@dataclass
+class AttnMeta:
+    """Device-side metadata of one step (see csrc/core/scheduler.h Batch)."""
+    num_seqs: int
+    num_decode_seqs: int
+    num_tokens: int
+    max_q_len: int
+    max_seq_len: int
+    positions: torch.Tensor
+    slot_mapping: torch.Tensor
+    q_start: torch.Tensor
+    seq_lens: torch.Tensor
+    block_tables: torch.Tensor
+    logits_idx: torch.Tensor
+    decode_splits: int = 1
+    decode_workspace: Optional[torch.Tensor] = None
+
+
+class TPGroup:
+    """Tensor-parallel group handle used by the model. Single-rank default."""
+
+    def __init__(self, rank: int = 0, size: int = 1):
+        self.rank = rank
+        self.size = size
+
+    def reduce(self, x: torch.Tensor) -> torch.Tensor:
+        """Sum partial activations across ranks (row-parallel output)."""
+        return x
+
+    def gather_vocab(self, x: torch.Tensor) -> torch.Tensor:
+        """Concatenate vocab-parallel logits along the last dim."""
+        return x
+
+
+def _shard(n: int, rank: int, size: int):
+    if n % size:
+        raise ValueError(f"dimension {n} not divisible by tensor-parallel size {size}")
+    s = n // size
+    return rank * s, (rank + 1) * s
+
+
+def tensor_id(name: str) -> int:
+    return zlib.crc32(name.encode()) & 0x7FFFFFFF
+
+
+class DecoderModel:
+    def __init__(self, cfg: ModelConfig, dtype: torch.dtype, device: torch.device,
+                 tp: Optional[TPGroup] = None, max_pos: Optional[int] = None):
+        self.cfg = cfg
+        self.dtype = dtype
+        self.device = torch.device(device)
+        self.tp = tp or TPGroup()
+        r, n = self.tp.rank, self.tp.size
+        if cfg.num_heads % n:
+            raise ValueError("num_heads must be divisible by tensor_parallel_size")
+        self.local_heads = cfg.num_heads // n
+        # KV heads: split when possible, else replicate (MQA / small GQA)
+        if cfg.num_kv_heads % n == 0:
+            self.local_kv_heads = cfg.num_kv_heads // n
+            self.kv_head_start = r * self.local_kv_heads
+        else:
+            if n % cfg.num_kv_heads:
+                raise ValueError("kv heads must divide or be divisible by tensor_parallel_size")
+            self.local_kv_heads = 1
+            self.kv_head_start = r * cfg.num_kv_heads // n
+        self.local_inter = cfg.intermediate_size // n
+        if cfg.intermediate_size % n:
+            raise ValueError("intermediate_size must be divisible by tensor_parallel_size")
+        self.vocab_start, self.vocab_end = 0, cfg.vocab_size
+        if n > 1 and cfg.vocab_size % n == 0:
+            self.vocab_start, self.vocab_end = _shard(cfg.vocab_size, r, n)
+        self.scale = 1.0 / math.sqrt(cfg.head_dim)
+        self.max_pos = max_pos or cfg.max_position_embeddings
+        self.cos_sin = cos_sin_table(cfg.rotary_dim, cfg.rope_theta, self.max_pos,
+                                     cfg.rope_scaling, device=self.device)
+        self.layers: List[SimpleNamespace] = []
+        self.embed = None
+        self.norm_w = None
+        self.norm_b = None
+        self.lm_head = None
+        self.lm_head_b = None
+
+    # ------------------------------------------------------------ weights
+    def _alloc(self, *shape, dtype=None):
+        return torch.empty(*shape, dtype=dtype or self.dtype, device=self.device)
+
+    def allocate(self) -> None:
+        c = self.cfg
+        H, D = c.hidden_size, c.head_dim
+        qkv_rows = (self.local_heads + 2 * self.local_kv_heads) * D
+        self.embed = self._alloc(c.vocab_size, H)
+        self.layers = []
+        for _ in range(c.num_layers):
+            L = SimpleNamespace()
+            L.ln1 = self._alloc(H)
+            L.ln1_b = self._alloc(H) if c.norm_type == "layernorm" else None
+            L.wqkv = self._alloc(qkv_rows, H)
+            L.bqkv = self._alloc(qkv_rows) if c.attention_bias else None
+            L.wo = self._alloc(H, self.local_heads * D)
+            L.bo = self._alloc(H) if c.norm_type == "layernorm" else None
+            if not c.parallel_block:
+                L.ln2 = self._alloc(H)
+                L.ln2_b = None
+            if c.num_experts:
+                L.router = self._alloc(c.num_experts, H)
+                L.w13 = self._alloc(c.num_experts, 2 * self.local_inter, H)
+                L.w2 = self._alloc(c.num_experts, H, self.local_inter)
+            elif c.hidden_act.startswith("gelu"):
+                L.w1 = self._alloc(self.local_inter, H)
+                L.b1 = self._alloc(self.local_inter) if c.mlp_bias else None
+                L.w2 = self._alloc(H, self.local_inter)
+                L.b2 = self._alloc(H) if c.mlp_bias else None
+            else:
+                L.w13 = self._alloc(2 * self.local_inter, H)
+                L.w2 = self._alloc(H, self.local_inter)
+            self.layers.append(L)
+        self.norm_w = self._alloc(H)
+        self.norm_b = self._alloc(H) if c.norm_type == "layernorm" else None
+        self.lm_head = self._alloc(self.vocab_end - self.vocab_start, H)
+        self.lm_head_b = self._alloc(self.vocab_end - self.vocab_start) if c.architecture == "phi" else None
+
+    def named_parameters(self):
+        yield "embed", self.embed
+        for i, L in enumerate(self.layers):
+            for k, v in vars(L).items():
+                if v is not None:
+                    yield f"layers.{i}.{k}", v
+        yield "norm", self.norm_w
+        if self.norm_b is not None:
+            yield "norm_b", self.norm_b
+        yield "lm_head", self.lm_head
+        if self.lm_head_b is not None:
+            yield "lm_head_b", self.lm_head_b
+
+    def init_dummy(self, seed: int = 0, std: float = 0.02) -> None:
+        """Random N(0, std) init (norm weights 1, biases small); each rank's
+        shard equals the matching slice of the single-rank tensor."""
+        from ..parallel.dummy_init import fill_normal_sharded
+        for name, t in self.named_parameters():
+            leaf = name.split(".")[-1]
+            if leaf in ("ln1", "ln2", "norm"):
+                t.fill_(1.0)
+                continue
+            if leaf in ("ln1_b", "ln2_b", "norm_b"):
+                t.zero_()
+                continue
+            fill_normal_sharded(t, self._full_spec(name, t), seed, tensor_id(name), std)
+
+    def _full_spec(self, name: str, t: torch.Tensor):
+        """(full_rows, full_cols, [(local_row_lo, full_row_lo, n)], col_lo) describing
+        where this rank's shard sits inside the single-rank tensor, used so the
+        dummy init is TP-invariant. Returns None for replicated tensors."""
+        c = self.cfg
+        r, n = self.tp.rank, self.tp.size
+        D = c.head_dim
+        leaf = name.split(".")[-1]
+        if n == 1:
+            return None
+        if leaf in ("wqkv", "bqkv"):
+            q0 = self.tp.rank * self.local_heads * D
+            k0 = c.num_heads * D + self.kv_head_start * D
+            v0 = (c.num_heads + c.num_kv_heads) * D + self.kv_head_start * D
+            nq, nkv = self.local_heads * D, self.local_kv_heads * D
+            full_rows = (c.num_heads + 2 * c.num_kv_heads) * D
+            return ("rows", full_rows, [(0, q0, nq), (nq, k0, nkv), (nq + nkv, v0, nkv)])
+        if leaf == "w13" and not c.num_experts:
+            I = c.intermediate_size
+            i0 = r * self.local_inter
+            return ("rows", 2 * I, [(0, i0, self.local_inter),
+                                    (self.local_inter, I + i0, self.local_inter)])
+        if leaf == "w13" and c.num_experts:
+            I = c.intermediate_size
+            i0 = r * self.local_inter
+            return ("rows3", 2 * I, [(0, i0, self.local_inter),
+                                     (self.local_inter, I + i0, self.local_inter)])
+        if leaf in ("w1", "b1"):
+            return ("rows", c.intermediate_size, [(0, r * self.local_inter, self.local_inter)])
+        if leaf == "wo":
+            return ("cols", c.num_heads * D, r * self.local_heads * D)
+        if leaf == "w2":
+            if c.num_experts:
+                return ("cols3", c.intermediate_size, r * self.local_inter)
+            return ("cols", c.intermediate_size, r * self.local_inter)
+        if leaf in ("lm_head", "lm_head_b") and self.vocab_end - self.vocab_start != c.vocab_size:
+            return ("rows", c.vocab_size, [(0, self.vocab_start, self.vocab_end - self.vocab_start)])
+        return None
+
+    def load_state(self, get: Callable[[str], Optional[torch.Tensor]]) -> None:
+        """Fill weights from full (unsharded) HF-named tensors; ``get`` returns a
+        CPU tensor or None. Slices the rank's shard before copying to device."""
+        from .weights import load_hf_weights
+        load_hf_weights(self, get)
+
+    # ------------------------------------------------------------ forward
+    def _norm(self, x, w, b, residual=None):
+        if self.cfg.norm_type == "layernorm":
+            return ops.layer_norm(x, w, b, self.cfg.rms_norm_eps, residual)
+        return ops.rms_norm(x, w, self.cfg.rms_norm_eps, residual)
+
+    def _attention(self, i: int, L, x: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor):
+        c = self.cfg
+        qkv = ops.linear(x, L.wqkv)
+        q = ops.qkv_rope_cache(qkv, meta.positions, self.cos_sin, kv_cache, i, meta.slot_mapping,
+                               self.local_heads, self.local_kv_heads, c.head_dim, c.rotary_dim,
+                               L.bqkv)
+        a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
+        o = ops.linear(a.reshape(a.shape[0], -1), L.wo)
+        return o
+
+    def _mlp(self, L, x: torch.Tensor) -> torch.Tensor:
+        c = self.cfg
+        if c.num_experts:
+            from ..parallel.moe import moe_forward
+            return moe_forward(self, L, x)
+        if c.hidden_act.startswith("gelu"):
+            h = ops.linear(x, L.w1, L.b1)
+            h = ops.gelu_tanh(h)
+            return ops.linear(h, L.w2)
+        h = ops.linear(x, L.w13)
+        h = ops.silu_and_mul(h)
+        return ops.linear(h, L.w2)
+
+    def forward(self, input_ids: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor) -> torch.Tensor:
+        """Returns final hidden states of the rows in ``meta.logits_idx``."""
+        c = self.cfg
+        h = ops.embedding(input_ids, self.embed)
+        residual = None
+        for i, L in enumerate(self.layers):
+            if c.parallel_block:
+                x, _ = self._norm(h, L.ln1, L.ln1_b)
+                a = self._attention(i, L, x, meta, kv_cache)
+                m = self._mlp(L, x)
+                s = a + m
+                if self.tp.rank == 0:  # row-parallel biases are added once
+                    if L.bo is not None:
+                        s = s + L.bo
+                    if getattr(L, "b2", None) is not None:
+                        s = s + L.b2
+                s = self.tp.reduce(s)
+                h = h + s
+                continue
+            x, residual = self._norm(h, L.ln1, L.ln1_b, residual)
+            a = self.tp.reduce(self._attention(i, L, x, meta, kv_cache))
+            x, residual = self._norm(a, L.ln2, L.ln2_b, residual)
+            h = self.tp.reduce(self._mlp(L, x))
+        if c.parallel_block:
+            last = h.index_select(0, meta.logits_idx)
+            x, _ = self._norm(last, self.norm_w, self.norm_b)
+            return x
+        # only the sampled rows need the final norm and the LM head
+        last_h = h.index_select(0, meta.logits_idx)
+        last_r = residual.index_select(0, meta.logits_idx)
+        x, _ = self._norm(last_h, self.norm_w, self.norm_b, last_r)
+        return x
+
+    def compute_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """fp32 logits over the full vocabulary (gathered across ranks)."""
+        logits = ops.linear(x, self.lm_head, self.lm_head_b).float()
+        if self.vocab_end - self.vocab_start != self.cfg.vocab_size:
+            logits = self.tp.gather_vocab(logits)
+        return logits

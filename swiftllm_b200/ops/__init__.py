@@ -1,0 +1,180 @@
+"""Hot ops. CUDA tensors go to the sm_100a kernels in ``swiftllm_b200._C``;
+CPU tensors go to the plain PyTorch restatements in :mod:`.reference` (the
+numerics oracle and the CPU runner). A CUDA tensor never falls back: if the
+extension is missing the call raises.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Optional, Tuple
+
+import torch
+
+from . import reference as ref
+
+_C = None
+_C_ERR: Optional[BaseException] = None
+try:  # the extension is built in-tree by setup.py / __graft_entry__.build()
+    from .. import _C as _C  # type: ignore
+except Exception as e:  # pragma: no cover - depends on the build
+    _C_ERR = e
+
+
+def cuda_ext():
+    """The compiled kernel module; raises loudly if it is not built."""
+    if _C is None:
+        raise RuntimeError(
+            "swiftllm_b200._C (sm_100a kernels) is not built or failed to load: "
+            f"{_C_ERR!r}. Run `python setup.py build_ext --inplace`.")
+    return _C
+
+
+def has_cuda_ext() -> bool:
+    return _C is not None
+
+
+# GEMM backend for CUDA tensors: "tcgen05" (our kernel, default) or "cublas"
+# (torch.matmul; only the NCCL+cuBLAS baseline path selects it).
+_GEMM_BACKEND = os.environ.get("SWIFTLLM_GEMM", "tcgen05")
+
+
+def set_gemm_backend(name: str) -> None:
+    global _GEMM_BACKEND
+    if name not in ("tcgen05", "cublas"):
+        raise ValueError(name)
+    _GEMM_BACKEND = name
+
+
+def gemm_backend() -> str:
+    return _GEMM_BACKEND
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
+             residual: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    if not x.is_cuda:
+        return ref.rms_norm(x, w, eps, residual)
+    C = cuda_ext()
+    out = torch.empty_like(x)
+    if residual is None:
+        C.rms_norm(out, x, w, eps)
+        return out, x
+    C.fused_add_rms_norm(out, x, residual, w, eps)  # residual updated in place
+    return out, residual
+
+
+def layer_norm(x, w, b, eps, residual=None):
+    if not x.is_cuda:
+        return ref.layer_norm(x, w, b, eps, residual)
+    C = cuda_ext()
+    out = torch.empty_like(x)
+    if residual is None:
+        C.layer_norm(out, x, w, b, eps)
+        return out, x
+    C.fused_add_layer_norm(out, x, residual, w, b, eps)
+    return out, residual
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.linear(x, w, b)
+    if _GEMM_BACKEND == "cublas":
+        y = torch.nn.functional.linear(x, w, b)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    C = cuda_ext()
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)
+    C.gemm(out, x, w, b)
+    return out
+
+
+def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.silu_and_mul(x)
+    out = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
+    cuda_ext().silu_and_mul(out, x)
+    return out
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.gelu_tanh(x)
+    out = torch.empty_like(x)
+    cuda_ext().gelu_tanh(out, x)
+    return out
+
+
+def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0) -> torch.Tensor:
+    """Rows of ``w`` for ``ids``; with ``vocab_start`` (vocab-parallel shard)
+    ids outside [vocab_start, vocab_start + rows) give zero rows."""
+    if not ids.is_cuda:
+        local = ids.long() - vocab_start
+        ok = (local >= 0) & (local < w.shape[0])
+        out = w[local.clamp(0, w.shape[0] - 1)].clone()
+        out[~ok] = 0
+        return out
+    out = torch.empty((ids.shape[0], w.shape[1]), dtype=w.dtype, device=w.device)
+    cuda_ext().embedding(out, ids, w, vocab_start)
+    return out
+
+
+def qkv_rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
+                   kv_cache: torch.Tensor, layer: int, slot_mapping: torch.Tensor,
+                   num_heads: int, num_kv_heads: int, head_dim: int, rotary_dim: int,
+                   bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Split packed qkv [T, (Hq + 2 Hkv) D], add bias, rotate q and k (neox),
+    write k and v into the paged cache at ``slot_mapping``; returns q
+    [T, Hq, D]."""
+    T = qkv.shape[0]
+    if not qkv.is_cuda:
+        if bias is not None:
+            qkv = (qkv.float() + bias.float()).to(qkv.dtype)
+        q = qkv[:, :num_heads * head_dim].reshape(T, num_heads, head_dim)
+        k = qkv[:, num_heads * head_dim:(num_heads + num_kv_heads) * head_dim]
+        k = k.reshape(T, num_kv_heads, head_dim)
+        v = qkv[:, (num_heads + num_kv_heads) * head_dim:].reshape(T, num_kv_heads, head_dim)
+        q = ref.apply_rope(q, positions, cos_sin, rotary_dim)
+        k = ref.apply_rope(k, positions, cos_sin, rotary_dim)
+        ref.write_kv(kv_cache[:, layer, 0], kv_cache[:, layer, 1], k, v, slot_mapping)
+        return q
+    q = torch.empty((T, num_heads, head_dim), dtype=qkv.dtype, device=qkv.device)
+    cuda_ext().qkv_rope_cache(q, qkv, positions, cos_sin, kv_cache, layer, slot_mapping,
+                              num_heads, num_kv_heads, head_dim, rotary_dim, bias)
+    return q
+
+
+def attention(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, meta,
+              scale: float, sliding_window: Optional[int] = None) -> torch.Tensor:
+    """Paged attention for a mixed batch: rows [0, num_decode) are single-token
+    decode queries, the rest are (chunked) prefills reading the cached prefix.
+    """
+    if not q.is_cuda:
+        return ref.paged_attention(q, kv_cache[:, layer, 0], kv_cache[:, layer, 1],
+                                   meta.block_tables, meta.q_start, meta.seq_lens, scale,
+                                   sliding_window)
+    C = cuda_ext()
+    out = torch.empty_like(q)
+    win = int(sliding_window or 0)
+    nd = meta.num_decode_seqs
+    if nd > 0:
+        C.paged_decode(out, q, kv_cache, layer, meta.block_tables, meta.seq_lens, nd,
+                       meta.decode_splits, scale, win, meta.decode_workspace)
+    if meta.num_seqs > nd:
+        C.paged_prefill(out, q, kv_cache, layer, meta.block_tables, meta.q_start,
+                        meta.seq_lens, nd, meta.num_seqs, meta.max_q_len, scale, win)
+    return out
+
+
+def copy_blocks(kv_cache: torch.Tensor, pairs: torch.Tensor) -> None:
+    """Copy whole KV blocks (all layers) src -> dst; pairs int32 [n, 2]."""
+    if pairs.numel() == 0:
+        return
+    if not kv_cache.is_cuda:
+        p = pairs.long()
+        kv_cache[p[:, 1]] = kv_cache[p[:, 0]]
+        return
+    cuda_ext().copy_blocks(kv_cache, pairs)

@@ -1,0 +1,128 @@
+"""Batch sampler used by the engine each step.
+
+Per sample row: penalties (if the batch has any) -> temperature -> min-p ->
+top-k -> top-p -> Philox draw, on the GPU in one fused kernel
+(``_C.sample``); on CPU tensors the same maths runs row by row through the
+C++ oracle (``_core.sample_row``). The uniform draw of row r is
+Philox4x32-10(key, counter) with
+  key = (seed, 0x5EED), counter = (step_idx, 0)     for seeded requests,
+  key = (engine seed, 0xA11), counter = (step, r)   otherwise,
+so seeded requests are reproducible regardless of batch composition.
+"""
+
+from __future__ import annotations
+
+from typing import Callable, List, Optional, Tuple
+
+import numpy as np
+import torch
+
+from .. import _core
+from ..parallel.dummy_init import mix_key
+
+
+def row_keys(seed: np.ndarray, step_idx: np.ndarray, engine_seed: int,
+             step: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """(key uint64, c0 uint32, c1 uint32) per row."""
+    n = seed.shape[0]
+    keys = np.empty(n, dtype=np.uint64)
+    c0 = np.empty(n, dtype=np.uint32)
+    c1 = np.empty(n, dtype=np.uint32)
+    seeded = seed >= 0
+    ekey = mix_key(engine_seed, 0xA11)
+    for i in range(n):
+        if seeded[i]:
+            keys[i] = mix_key(int(seed[i]), 0x5EED)
+            c0[i] = int(step_idx[i]) & 0xFFFFFFFF
+            c1[i] = 0
+        else:
+            keys[i] = ekey
+            c0[i] = step & 0xFFFFFFFF
+            c1[i] = i
+    return keys, c0, c1
+
+
+class BatchSampler:
+    def __init__(self, vocab_size: int, engine_seed: int, device: torch.device):
+        self.vocab = vocab_size
+        self.seed = engine_seed
+        self.device = torch.device(device)
+        self.step = 0
+
+    def _penalize(self, logits: torch.Tensor, b, rows: np.ndarray,
+                  history: Callable[[int], Tuple[np.ndarray, np.ndarray]]) -> torch.Tensor:
+        """Apply repetition/frequency/presence penalties to the logits rows of
+        ``rows``; history(seq_id) -> (prompt_ids, output_ids)."""
+        rep = np.asarray(b.repetition_penalty)
+        pres = np.asarray(b.presence_penalty)
+        freq = np.asarray(b.frequency_penalty)
+        lidx = np.asarray(b.sample_logit_idx)
+        tgt = np.asarray(b.sample_target_seq)
+        out = logits[torch.from_numpy(lidx.astype(np.int64)).to(logits.device)].clone()
+        seq_ids = np.asarray(b.seq_ids)
+        srow = np.asarray(b.sample_seq_row)
+        for r in range(out.shape[0]):
+            if rep[r] == 1.0 and pres[r] == 0.0 and freq[r] == 0.0:
+                continue
+            sid = int(tgt[r]) if tgt[r] >= 0 else int(seq_ids[srow[r]])
+            prompt, output = history(sid)
+            V = out.shape[1]
+            row = out[r]
+            if rep[r] != 1.0:
+                seen = np.unique(np.concatenate([prompt, output]).astype(np.int64))
+                seen = seen[(seen >= 0) & (seen < V)]
+                if seen.size:
+                    idx = torch.from_numpy(seen).to(row.device)
+                    v = row[idx]
+                    row[idx] = torch.where(v > 0, v / float(rep[r]), v * float(rep[r]))
+            if output.size and (pres[r] != 0.0 or freq[r] != 0.0):
+                t, c = np.unique(output.astype(np.int64), return_counts=True)
+                ok = (t >= 0) & (t < V)
+                idx = torch.from_numpy(t[ok]).to(row.device)
+                cnt = torch.from_numpy(c[ok].astype(np.float32)).to(row.device)
+                row.index_add_(0, idx, -(float(freq[r]) * cnt + float(pres[r])))
+        return out
+
+    def __call__(self, logits: torch.Tensor, b,
+                 history: Optional[Callable[[int], Tuple[np.ndarray, np.ndarray]]] = None
+                 ) -> Tuple[np.ndarray, np.ndarray]:
+        """Returns (tokens int32 [rows], logprobs float32 [rows])."""
+        self.step += 1
+        n = int(b.num_sample_rows)
+        if n == 0:
+            return np.zeros(0, np.int32), np.zeros(0, np.float32)
+        lidx = np.asarray(b.sample_logit_idx, dtype=np.int32)
+        if b.any_penalty and history is not None:
+            rows_logits = self._penalize(logits, b, lidx, history)
+            lidx = np.arange(n, dtype=np.int32)
+        else:
+            rows_logits = logits
+        temp = np.asarray(b.temperature, dtype=np.float32)
+        top_p = np.asarray(b.top_p, dtype=np.float32)
+        top_k = np.asarray(b.top_k, dtype=np.int32)
+        min_p = np.asarray(b.min_p, dtype=np.float32)
+        keys, c0, c1 = row_keys(np.asarray(b.seed), np.asarray(b.step_idx), self.seed, self.step)
+        if rows_logits.is_cuda:
+            from ..ops import cuda_ext
+            C = cuda_ext()
+            f = torch.from_numpy(np.stack([temp, top_p, min_p]).astype(np.float32))
+            i = torch.from_numpy(np.stack([lidx, top_k, c0.view(np.int32), c1.view(np.int32)]))
+            k = torch.from_numpy(keys.view(np.int64))
+            dev = rows_logits.device
+            tokens = torch.empty(n, dtype=torch.int32, device=dev)
+            lps = torch.empty(n, dtype=torch.float32, device=dev)
+            C.sample(tokens, lps, rows_logits, f.to(dev, non_blocking=True),
+                     i.to(dev, non_blocking=True), k.to(dev, non_blocking=True),
+                     bool(b.any_random))
+            both = torch.stack([tokens.view(torch.float32), lps]).cpu().numpy()
+            return both[0].view(np.int32).copy(), both[1].copy()
+        lg = rows_logits.float().numpy()
+        toks = np.empty(n, dtype=np.int32)
+        lps = np.empty(n, dtype=np.float32)
+        for r in range(n):
+            u = _core.philox_uniform(int(keys[r]), int(c0[r]), int(c1[r]))
+            p = _core.SampleParams(temperature=float(temp[r]), top_p=float(top_p[r]),
+                                   top_k=int(top_k[r]), min_p=float(min_p[r]))
+            t, lp = _core.sample_row(lg[lidx[r]], p, u)
+            toks[r], lps[r] = t, lp
+        return toks, lps
