@@ -1,0 +1,55 @@
+// torch extension module swiftllm_b200._C: the sm_100a kernels.
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace swift {
+void rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, double eps);
+void fused_add_rms_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residual, torch::Tensor w,
+                        double eps);
+void layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b,
+                double eps);
+void fused_add_layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor residual,
+                          torch::Tensor w, c10::optional<torch::Tensor> b, double eps);
+void silu_and_mul(torch::Tensor out, torch::Tensor x);
+void gelu_tanh(torch::Tensor out, torch::Tensor x);
+void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor w, int64_t vocab_start);
+void qkv_rope_cache(torch::Tensor q, torch::Tensor qkv, torch::Tensor positions,
+                    torch::Tensor cos_sin, torch::Tensor kv, int64_t layer, torch::Tensor slots,
+                    int64_t Hq, int64_t Hkv, int64_t D, int64_t rot,
+                    c10::optional<torch::Tensor> bias);
+void copy_blocks(torch::Tensor kv, torch::Tensor pairs);
+void init_normal(torch::Tensor v, int64_t key, double std, int64_t full_rows, int64_t full_cols,
+                 int64_t row0, int64_t col0);
+std::vector<int64_t> read_status(bool clear);
+int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
+                     torch::Tensor bt, torch::Tensor seq_lens, int64_t rows, int64_t splits,
+                     double scale, int64_t window, torch::Tensor ws);
+void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
+                   torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int64_t seq0,
+                   int64_t seq1, int64_t max_q_len, double scale, int64_t window);
+void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,
+            torch::Tensor iparams, torch::Tensor keys, bool any_random);
+int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
+std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
+}  // namespace swift
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "swiftllm_b200 sm_100a kernels";
+  m.def("rms_norm", &swift::rms_norm);
+  m.def("fused_add_rms_norm", &swift::fused_add_rms_norm);
+  m.def("layer_norm", &swift::layer_norm);
+  m.def("fused_add_layer_norm", &swift::fused_add_layer_norm);
+  m.def("silu_and_mul", &swift::silu_and_mul);
+  m.def("gelu_tanh", &swift::gelu_tanh);
+  m.def("embedding", &swift::embedding);
+  m.def("qkv_rope_cache", &swift::qkv_rope_cache);
+  m.def("copy_blocks", &swift::copy_blocks);
+  m.def("init_normal", &swift::init_normal);
+  m.def("read_status", &swift::read_status, pybind11::arg("clear") = true);
+  m.def("paged_decode", &swift::paged_decode);
+  m.def("paged_prefill", &swift::paged_prefill);
+  m.def("sample", &swift::sample);
+  m.def("gemm", &swift::gemm);
+  m.def("gemm_plan", &swift::gemm_plan);
+}

@@ -1,0 +1,205 @@
+// Fused sampling: temperature -> softmax -> min-p -> top-k -> top-p -> draw,
+// one CTA (1024 threads) per sample row, reading fp32 logits from L2.
+//
+// Replaces the reference's softmax / top_k_sampling / top_p_sampling stubs
+// (crates/swiftllm-cuda/src/bindings.rs:291-350). Same stage order, same
+// Philox4x32-10 stream and the same index-order inverse-CDF draw as the CPU
+// oracle (csrc/core/sampler.cpp), so seeded draws agree with it.
+//
+// Thresholds without sorting: the k-th largest probability (top-k) and the
+// smallest probability whose top mass reaches p (top-p) are found by radix
+// select over the bit pattern of the (positive) fp32 probability, three
+// passes of 11/11/10 bits with count or mass histograms in shared memory.
+#include "common.cuh"
+
+namespace swift {
+
+constexpr int kSampThreads = 1024;
+constexpr int kBins = 2048;
+
+struct ArgMax {
+  float v;
+  int i;
+};
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+
+// MASS=false: value of the k-th largest probability (k = target).
+// MASS=true: largest value v with sum_{p >= v, p >= floor} p >= target.
+template <bool MASS>
+__device__ float radix_select(const float* __restrict__ row, int V, float mx, float invT,
+                              float invZ, float floor_p, float target, int* hc, float* hm,
+                              float* scratch) {
+  uint32_t prefix = 0, pmask = 0;
+  const int shifts[3] = {21, 10, 0};
+  const int widths[3] = {11, 11, 10};
+  float rem = target;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int sh = shifts[pass], nb = 1 << widths[pass];
+    for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+      hc[b] = 0;
+      hm[b] = 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      float p = __expf((row[i] - mx) * invT) * invZ;
+      if (p < floor_p) continue;
+      uint32_t bits = __float_as_uint(p);
+      if ((bits & pmask) != prefix) continue;
+      int b = (bits >> sh) & (nb - 1);
+      if (MASS) atomicAdd(&hm[b], p);
+      else atomicAdd(&hc[b], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float acc = 0.f;
+      int pick = 0;
+      for (int b = nb - 1; b >= 0; --b) {
+        float c = MASS ? hm[b] : static_cast<float>(hc[b]);
+        pick = b;
+        if (acc + c >= rem) break;
+        acc += c;
+      }
+      scratch[0] = static_cast<float>(pick);
+      scratch[1] = rem - acc;
+    }
+    __syncthreads();
+    const uint32_t pick = static_cast<uint32_t>(scratch[0]);
+    rem = scratch[1];
+    prefix |= pick << sh;
+    pmask |= static_cast<uint32_t>(nb - 1) << sh;
+    __syncthreads();
+  }
+  return __uint_as_float(prefix);
+}
+
+__global__ void __launch_bounds__(kSampThreads)
+    sample_kernel(int32_t* __restrict__ tokens, float* __restrict__ lps,
+                  const float* __restrict__ logits, int64_t ld, int V, const float* __restrict__ fp,
+                  const int32_t* __restrict__ ip, const uint64_t* __restrict__ keys, int n) {
+  __shared__ int hc[kBins];
+  __shared__ float hm[kBins];
+  __shared__ float red[33];
+  __shared__ float scratch[4];
+  __shared__ ArgMax am[32];
+  __shared__ float csum[kSampThreads];
+  __shared__ int pick_s;
+  const int r = blockIdx.x;
+  const float temp = fp[r], top_p = fp[n + r], min_p = fp[2 * n + r];
+  const int lrow = ip[r], top_k = ip[n + r];
+  const uint32_t c0 = static_cast<uint32_t>(ip[2 * n + r]), c1 = static_cast<uint32_t>(ip[3 * n + r]);
+  const float* row = logits + int64_t(lrow) * ld;
+  const bool greedy = temp <= 0.f || top_k == 1;
+  const float invT = greedy ? 1.f : 1.f / temp;
+
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{row[i], i});
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+    best = better(best, other);
+  }
+  if ((threadIdx.x & 31) == 0) am[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    best = threadIdx.x < (blockDim.x >> 5) ? am[threadIdx.x] : ArgMax{-INFINITY, 0x7fffffff};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+      best = better(best, other);
+    }
+    if (threadIdx.x == 0) am[0] = best;
+  }
+  __syncthreads();
+  const float mx = am[0].v;
+  const int arg = am[0].i;
+  float z = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) z += __expf((row[i] - mx) * invT);
+  z = block_sum(z, red);
+  const float logZ = logf(z);
+  if (greedy) {
+    if (threadIdx.x == 0) {
+      tokens[r] = arg;
+      lps[r] = -logZ;
+    }
+    return;
+  }
+  const float invZ = 1.f / z;
+  float thresh = min_p > 0.f ? min_p * invZ : 0.f;  // p(argmax) = 1 / Z
+  if (top_k > 0 && top_k < V)
+    thresh = fmaxf(thresh, radix_select<false>(row, V, mx, invT, invZ, 0.f,
+                                               static_cast<float>(top_k), hc, hm, scratch));
+  if (top_p < 1.f) {
+    float mass = 0.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      float p = __expf((row[i] - mx) * invT) * invZ;
+      if (p >= thresh) mass += p;
+    }
+    mass = block_sum(mass, red);
+    thresh = fmaxf(thresh, radix_select<true>(row, V, mx, invT, invZ, thresh, top_p * mass, hc,
+                                              hm, scratch));
+  }
+  // inverse CDF in vocabulary order over the kept set
+  const int per = (V + blockDim.x - 1) / blockDim.x;
+  const int lo = threadIdx.x * per, hi = min(V, lo + per);
+  float part = 0.f;
+  for (int i = lo; i < hi; ++i) {
+    float p = __expf((row[i] - mx) * invT) * invZ;
+    if (p >= thresh) part += p;
+  }
+  csum[threadIdx.x] = part;
+  if (threadIdx.x == 0) pick_s = 0x7fffffff;
+  __syncthreads();
+  for (int off = 1; off < blockDim.x; off <<= 1) {  // inclusive Hillis-Steele scan
+    float v = threadIdx.x >= off ? csum[threadIdx.x - off] : 0.f;
+    __syncthreads();
+    csum[threadIdx.x] += v;
+    __syncthreads();
+  }
+  const float total = csum[blockDim.x - 1];
+  uint32_t o[4];
+  philox4x32(keys[r], c0, c1, 0, 0, o);
+  const float u = static_cast<float>(o[0] >> 8) * (1.0f / 16777216.0f);
+  const float target = u * total;
+  const float before = threadIdx.x ? csum[threadIdx.x - 1] : 0.f;
+  if (part > 0.f && target >= before &&
+      (target < csum[threadIdx.x] || threadIdx.x == blockDim.x - 1 || csum[threadIdx.x] >= total)) {
+    float c = before;
+    int pick = -1;
+    for (int i = lo; i < hi; ++i) {
+      float p = __expf((row[i] - mx) * invT) * invZ;
+      if (p < thresh) continue;
+      c += p;
+      pick = i;
+      if (c > target) break;
+    }
+    if (pick >= 0) atomicMin(&pick_s, pick);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int pick = pick_s;
+    if (pick == 0x7fffffff) pick = arg;
+    tokens[r] = pick;
+    lps[r] = (row[pick] - mx) * invT - logZ;
+  }
+}
+
+// fparams [3, n] = (temperature, top_p, min_p); iparams [4, n] = (logit row,
+// top_k, counter0, counter1); keys [n] (int64 holding the uint64 Philox key).
+void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,
+            torch::Tensor iparams, torch::Tensor keys, bool /*any_random*/) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1);
+  TORCH_CHECK(fparams.scalar_type() == at::kFloat && iparams.scalar_type() == at::kInt);
+  TORCH_CHECK(keys.scalar_type() == at::kLong);
+  const int n = static_cast<int>(tokens.numel());
+  if (!n) return;
+  sample_kernel<<<n, kSampThreads, 0, cur_stream()>>>(
+      tokens.data_ptr<int32_t>(), lps.data_ptr<float>(), logits.data_ptr<float>(), logits.stride(0),
+      static_cast<int>(logits.size(1)), fparams.data_ptr<float>(), iparams.data_ptr<int32_t>(),
+      reinterpret_cast<const uint64_t*>(keys.data_ptr<int64_t>()), n);
+  SWIFT_CHECK_LAUNCH();
+}
+
+}  // namespace swift
