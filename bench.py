@@ -1,0 +1,240 @@
+"""Headline benchmark: output tokens/s of offline continuous batching on the
+Llama-2-7B architecture (bf16, random init), tensor parallel over N GPUs.
+
+Workload: 1000 requests of uniform-random token ids,
+input lengths U[128, 1024], output lengths U[128, 512], seed 0, EOS ignored,
+greedy decoding, KV block 16, gpu_memory_utilization 0.9.
+
+One "step" is one engine iteration (schedule -> forward over the whole
+continuous batch -> fused sampling -> scheduler update). The full workload
+runs through the public API (``LLM.generate``): that is the end-to-end
+number ("e2e"; every step copies its packed inputs host->device from pinned
+memory and reads the sampled tokens back). Inside that run, once the batch
+first fills to max_num_seqs and W more warm-up steps have run, K steps are
+timed on the device (barrier + synchronize on both sides, CUDA events, max
+over ranks): that is ``value``. Decode steps stream the 13.5 GB of weights
+and the KV pool, far more than the 126 MB L2, so no L2 flush is needed.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+For N > 1 run under torchrun (one rank per GPU); rank 0 prints one JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "output tok/s at Llama-2-7B/70B TP1-8 (max over ranks); p50 TTFT & TPOT"
+MODEL = "llama-2-7b"
+
+
+def workload(n_req: int, seed: int = 0):
+    rng = np.random.default_rng(seed)
+    ins = rng.integers(128, 1025, size=n_req)
+    outs = rng.integers(128, 513, size=n_req)
+    prompts = [rng.integers(0, 32000, size=int(i)).tolist() for i in ins]
+    return prompts, [int(o) for o in outs]
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed window."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+        self.th = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.th = threading.Thread(target=self._read, daemon=True)
+        self.th.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.th:
+            self.th.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        med = float(np.median(sm)) if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def reference_arm(args) -> None:
+    msg = ("reference cannot be installed or run: its pyproject needs the maturin (Rust) build "
+           "backend, absent offline, and its forward pass returns zeros / canned text "
+           "(crates/swiftllm-models/src/layers/mod.rs:65-78, python/swiftllm/engine.py:351-384)")
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": msg}))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=1000)
+    ap.add_argument("--model", default=MODEL)
+    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    args.warmup = max(args.warmup, 3)
+    os.environ["SWIFTLLM_GEMM"] = args.gemm
+    import torch
+    from swiftllm_b200 import LLM, SamplingParams
+    from swiftllm_b200.config import EngineConfig
+    from swiftllm_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    ekw = dict(load_format="dummy", dtype="bfloat16", tensor_parallel_size=args.gpus,
+               gpu_memory_utilization=0.9, block_size=16, max_num_seqs=args.max_num_seqs,
+               enable_chunked_prefill=True, max_num_batched_tokens=8192, max_model_len=2048,
+               comm_backend=args.comm, seed=0, preemption_mode="recompute")
+    if rank != 0:
+        from swiftllm_b200.parallel.executor import run_worker_from_env
+        run_worker_from_env(EngineConfig(model=args.model, **ekw))
+        return
+
+    prompts, out_lens = workload(args.requests)
+    sps = [SamplingParams(temperature=0.0, max_tokens=o, ignore_eos=True) for o in out_lens]
+    t_init = time.time()
+    llm = LLM(args.model, **ekw)
+    eng = llm.llm_engine
+    eng._ensure_initialized()
+    init_s = time.time() - t_init
+    clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
+    st = {"filled": None, "start": None, "stop": None, "tok": 0, "launch0": 0, "launches": 0}
+
+    def hook(e):
+        s = e.num_steps
+        if st["filled"] is None and e.scheduler.num_running >= args.max_num_seqs:
+            st["filled"] = s
+        if st["filled"] is not None and st["start"] is None and s >= st["filled"] + args.warmup:
+            clocks.start()
+            e.executor.timer("start")
+            st["start"] = s
+            st["launch0"] = ops.LAUNCHES[0]
+            return
+        if st["start"] is not None and st["stop"] is None:
+            st["tok"] += e.last_step_tokens
+            if s >= st["start"] + args.steps:
+                e.executor.timer("stop")
+                st["stop"] = s
+                st["launches"] = ops.LAUNCHES[0] - st["launch0"]
+
+    eng.step_hook = hook
+    torch.cuda.synchronize()
+    io_before = list(eng.io_bytes)
+    steps_before = eng.num_steps
+    t0 = time.perf_counter()
+    outs = llm.generate(prompt_token_ids=prompts, sampling_params=sps, use_tqdm=False)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if st["start"] is not None and st["stop"] is None:  # workload ended inside the window
+        eng.executor.timer("stop")
+        st["stop"] = eng.num_steps
+        st["launches"] = ops.LAUNCHES[0] - st["launch0"]
+    clk = clocks.stop() if st["start"] is not None else {"sm_mhz": None, "reasons": ["no window"]}
+    ms = eng.executor.timer("report") if st["start"] is not None else None
+    n_out = sum(len(o.outputs[0].token_ids) for o in outs)
+    steps_total = eng.num_steps - steps_before
+    h2d = (eng.io_bytes[0] - io_before[0]) / max(steps_total, 1)
+    d2h = (eng.io_bytes[1] - io_before[1]) / max(steps_total, 1)
+    ttft = [o.metrics["ttft"] for o in outs if o.metrics and o.metrics["ttft"] is not None]
+    tpot = [o.metrics["tpot"] for o in outs if o.metrics and o.metrics["tpot"] is not None]
+    timed_steps = (st["stop"] - st["start"]) if st["start"] is not None else 0
+    value = st["tok"] / (ms / 1e3) if ms else None
+    e2e_value = n_out / e2e_s
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1) if value else None,
+        "unit": "output tokens/s",
+        "n_gpus": args.gpus,
+        "steps": timed_steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / max(timed_steps, 1), 3) if ms else None,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
+        "config": {
+            "model": "Llama-2-7B architecture (32L, H4096, 32 heads MHA, FFN 11008, V32000)",
+            "global_batch": args.max_num_seqs,
+            "seq_len": "in U[128,1024], out U[128,512]",
+            "requests": args.requests,
+            "parallelism": f"tp{args.gpus}",
+            "comm": args.comm if args.gpus > 1 else "none",
+            "gemm": args.gemm,
+            "l2": "no flush: each step streams weights + KV pool (>126 MB L2)",
+            "window": f"{timed_steps} engine steps starting {args.warmup} steps after the batch "
+                      f"first filled to {args.max_num_seqs} running sequences",
+        },
+        "e2e": {"value": round(e2e_value, 1),
+                "unit": "output tokens/s (LLM.generate, whole workload)",
+                "seconds": round(e2e_s, 2), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h), "engine_steps": steps_total,
+                "output_tokens": n_out},
+        "p50_ttft_ms": round(float(np.median(ttft)) * 1e3, 1) if ttft else None,
+        "p50_tpot_ms": round(float(np.median(tpot)) * 1e3, 2) if tpot else None,
+        "gpu_launches": int(st["launches"]),
+        "clocks": clk,
+        "init_s": round(init_s, 1),
+    }
+    print(json.dumps(res), flush=True)
+    llm.shutdown()
+
+
+if __name__ == "__main__":
+    main()

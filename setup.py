@@ -50,7 +50,7 @@ def cuda_ext():
         "swiftllm_b200._C", srcs,
         include_dirs=[os.path.join(PKG, "csrc", "kernels")],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": nvcc},
-        libraries=["cuda"])
+    )
 
 
 exts = []

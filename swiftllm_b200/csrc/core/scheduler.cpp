@@ -242,7 +242,23 @@ std::unique_ptr<Batch> Scheduler::schedule(double now) {
         if (s.status == SeqStatus::SWAPPED)
           need += bm_->blocks_needed(static_cast<int64_t>(s.tokens.size()) + extra);
       }
-      if (!bm_->can_allocate(need, true)) break;
+      if (!bm_->can_allocate(need, true)) {
+        if (running_.empty() && items.empty() &&
+            need > bm_->num_gpu_blocks() - bm_->watermark_blocks()) {
+          // can never come back: end it rather than wait forever
+          swapped_.pop_front();
+          for (int64_t sid : g.seqs) {
+            Sequence& s = seqs_.at(sid);
+            if (s.status != SeqStatus::SWAPPED) continue;
+            bm_->free(sid);
+            s.status = SeqStatus::FINISHED_LENGTH;
+          }
+          ++stats_.finished;
+          out->preempted_groups.push_back(-gid);
+          continue;
+        }
+        break;
+      }
       swapped_.pop_front();
       for (int64_t sid : g.seqs) {
         Sequence& s = seqs_.at(sid);
@@ -427,6 +443,17 @@ StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float*
                              double now) {
   StepResult res;
   std::vector<int64_t> touched;
+  // register newly full blocks for prefix caching before any sequence of this
+  // step finishes and returns its blocks
+  if (bm_->prefix_caching()) {
+    for (int64_t sid : b.seq_ids) {
+      auto it = seqs_.find(sid);
+      if (it == seqs_.end()) continue;
+      Sequence& s = it->second;
+      if (s.status == SeqStatus::RUNNING)
+        bm_->register_full_blocks(sid, s.tokens.data(), s.num_computed);
+    }
+  }
   const size_t rows = b.sample_logit_idx.size();
   // children (n > 1) fork from the parent's prompt before the parent appends
   std::vector<size_t> order;
@@ -489,16 +516,6 @@ StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float*
       s.status = fin;
     }
     touched.push_back(gid);
-  }
-  // register full blocks for prefix caching
-  if (bm_->prefix_caching()) {
-    for (int64_t sid : b.seq_ids) {
-      auto it = seqs_.find(sid);
-      if (it == seqs_.end()) continue;
-      Sequence& s = it->second;
-      if (s.status == SeqStatus::RUNNING)
-        bm_->register_full_blocks(sid, s.tokens.data(), s.num_computed);
-    }
   }
   std::sort(touched.begin(), touched.end());
   touched.erase(std::unique(touched.begin(), touched.end()), touched.end());

@@ -45,6 +45,25 @@ class _Req:
     done: bool = False
 
 
+def prepare_config(c: EngineConfig):
+    """Resolve the model and fill the derived engine settings (max_model_len,
+    max_num_batched_tokens). Every tensor-parallel rank calls this on the same
+    EngineConfig, so all ranks agree on shapes. Returns the ModelConfig."""
+    from ..model_resolver import resolve_model
+    from ..models.config import load_config
+    if c.load_format != "dummy":
+        c.model = resolve_model(c.model, download_dir=c.download_dir)
+    mcfg = load_config(c.model)
+    max_len = c.max_model_len or min(mcfg.max_position_embeddings, 4096)
+    c.max_model_len = max_len
+    if c.max_num_batched_tokens is None:
+        c.max_num_batched_tokens = max(max_len, 8192) if not c.enable_chunked_prefill \
+            else max(c.max_prefill_tokens, 2048)
+    if not c.enable_chunked_prefill and c.max_num_batched_tokens < max_len:
+        c.max_num_batched_tokens = max_len
+    return mcfg
+
+
 class LLMEngine:
     def __init__(self, config: EngineConfig):
         self.config = config
@@ -63,30 +82,25 @@ class LLMEngine:
         self._gen_tokens = 0
         self._prompt_tokens = 0
         self._aborted: List[str] = []
+        # instrumentation (bench): tokens of the last step, host<->device bytes
+        # moved by steps (h2d, d2h), step count and an optional per-step hook
+        self.last_step_tokens = 0
+        self.io_bytes = [0, 0]
+        self.num_steps = 0
+        self.step_hook = None
 
     # ------------------------------------------------------------ init
     def _ensure_initialized(self) -> None:
         if self._initialized:
             return
-        from ..model_resolver import resolve_model
-        from ..models.config import load_config
         from .tokenizer import load_tokenizer
         from ..parallel.executor import make_executor
         from ..sampling.batch import BatchSampler
         c = self.config
-        path = c.model
-        if c.load_format != "dummy":
-            path = resolve_model(c.model, download_dir=c.download_dir)
-            c.model = path
-        self.model_config = load_config(path)
+        self.model_config = prepare_config(c)
         mcfg = self.model_config
-        max_len = c.max_model_len or min(mcfg.max_position_embeddings, 4096)
-        c.max_model_len = max_len
-        if c.max_num_batched_tokens is None:
-            c.max_num_batched_tokens = max(max_len, 8192) if not c.enable_chunked_prefill \
-                else max(c.max_prefill_tokens, 2048)
-        if not c.enable_chunked_prefill and c.max_num_batched_tokens < max_len:
-            c.max_num_batched_tokens = max_len
+        path = c.model
+        max_len = c.max_model_len
         tok_path = c.tokenizer if c.tokenizer and c.tokenizer != "" else path
         self.tokenizer = load_tokenizer(tok_path, mcfg.vocab_size, c.trust_remote_code)
         self.eos_token_id = getattr(self.tokenizer, "eos_token_id", None)
@@ -203,6 +217,11 @@ class LLMEngine:
         si = step_input_from_batch(b)
         logits = self.executor.execute(si)
         if b.num_sample_rows == 0:
+            self.last_step_tokens = 0
+            self.io_bytes[0] += si.ints.nbytes
+            self.num_steps += 1
+            if self.step_hook is not None:
+                self.step_hook(self)
             return outs
         with nvtx.range("sample"):
             toks, lps = self.sampler(logits, b, self._history)
@@ -212,6 +231,12 @@ class LLMEngine:
             want_lp = self._top_logprobs(logits, b, toks)
         res = self.scheduler.update(b, toks, lps, time.monotonic())
         self._gen_tokens += len(res.token)
+        self.last_step_tokens = len(res.token)
+        self.io_bytes[0] += si.ints.nbytes + si.logits_idx.nbytes + 28 * int(b.num_sample_rows)
+        self.io_bytes[1] += 8 * int(b.num_sample_rows)
+        self.num_steps += 1
+        if self.step_hook is not None:
+            self.step_hook(self)
         return outs + self._process(res, want_lp)
 
     def _top_logprobs(self, logits, b, toks):

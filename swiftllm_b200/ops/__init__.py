@@ -50,16 +50,29 @@ def gemm_backend() -> str:
     return _GEMM_BACKEND
 
 
+# Number of our kernels launched through this module (CUDA-graph replays add
+# the count recorded at capture). Read by bench.py for "gpu_launches".
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += int(n)
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float,
              residual: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Returns (normed, residual). With ``residual`` it is updated in place to
+    residual + x first (fused add + RMSNorm)."""
     if not x.is_cuda:
         return ref.rms_norm(x, w, eps, residual)
     C = cuda_ext()
     out = torch.empty_like(x)
     if residual is None:
         C.rms_norm(out, x, w, eps)
+        _count()
         return out, x
-    C.fused_add_rms_norm(out, x, residual, w, eps)  # residual updated in place
+    C.fused_add_rms_norm(out, x, residual, w, eps)
+    _count()
     return out, residual
 
 
@@ -70,8 +83,10 @@ def layer_norm(x, w, b, eps, residual=None):
     out = torch.empty_like(x)
     if residual is None:
         C.layer_norm(out, x, w, b, eps)
+        _count()
         return out, x
     C.fused_add_layer_norm(out, x, residual, w, b, eps)
+    _count()
     return out, residual
 
 
@@ -88,7 +103,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     C = cuda_ext()
     if out is None:
         out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)
-    C.gemm(out, x, w, b)
+    _count(C.gemm(out, x, w, b))
     return out
 
 
@@ -97,6 +112,7 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
         return ref.silu_and_mul(x)
     out = torch.empty(x.shape[:-1] + (x.shape[-1] // 2,), dtype=x.dtype, device=x.device)
     cuda_ext().silu_and_mul(out, x)
+    _count()
     return out
 
 
@@ -105,6 +121,7 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
         return ref.gelu_tanh(x)
     out = torch.empty_like(x)
     cuda_ext().gelu_tanh(out, x)
+    _count()
     return out
 
 
@@ -119,6 +136,7 @@ def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0) -> torch
         return out
     out = torch.empty((ids.shape[0], w.shape[1]), dtype=w.dtype, device=w.device)
     cuda_ext().embedding(out, ids, w, vocab_start)
+    _count()
     return out
 
 
@@ -144,6 +162,7 @@ def qkv_rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
     q = torch.empty((T, num_heads, head_dim), dtype=qkv.dtype, device=qkv.device)
     cuda_ext().qkv_rope_cache(q, qkv, positions, cos_sin, kv_cache, layer, slot_mapping,
                               num_heads, num_kv_heads, head_dim, rotary_dim, bias)
+    _count()
     return q
 
 
@@ -161,11 +180,12 @@ def attention(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, meta,
     win = int(sliding_window or 0)
     nd = meta.num_decode_seqs
     if nd > 0:
-        C.paged_decode(out, q, kv_cache, layer, meta.block_tables, meta.seq_lens, nd,
-                       meta.decode_splits, scale, win, meta.decode_workspace)
+        _count(C.paged_decode(out, q, kv_cache, layer, meta.block_tables, meta.seq_lens, nd,
+                              meta.decode_splits, scale, win, meta.decode_workspace))
     if meta.num_seqs > nd:
         C.paged_prefill(out, q, kv_cache, layer, meta.block_tables, meta.q_start,
                         meta.seq_lens, nd, meta.num_seqs, meta.max_q_len, scale, win)
+        _count()
     return out
 
 
@@ -178,3 +198,4 @@ def copy_blocks(kv_cache: torch.Tensor, pairs: torch.Tensor) -> None:
         kv_cache[p[:, 1]] = kv_cache[p[:, 0]]
         return
     cuda_ext().copy_blocks(kv_cache, pairs)
+    _count()

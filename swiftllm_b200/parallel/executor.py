@@ -81,8 +81,74 @@ def worker_loop(model_cfg, cfg, rank: int, world: int, local_rank: int, channel_
         msg = ch.receive(timeout=-1.0, peer_timeout=STEP_TIMEOUT)
         if msg == _SHUTDOWN:
             break
-        si = pickle.loads(msg)
-        runner.execute(si)
+        obj = pickle.loads(msg)
+        if isinstance(obj, tuple):  # control message: ("timer", "start" | "stop" | "report")
+            _timer_op(runner, obj[1])
+            continue
+        runner.execute(obj)
+
+
+def run_worker_from_env(cfg) -> None:
+    """Entry for ranks != 0 of a torchrun job (bench.py): join the process
+    group, build this rank's runner and serve rank 0's steps until shutdown."""
+    from ..engine.llm_engine import prepare_config
+    model_cfg = prepare_config(cfg)
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    local_rank = int(os.environ.get("LOCAL_RANK", rank))
+    backend = "nccl" if cfg.device != "cpu" and torch.cuda.is_available() else "gloo"
+    init_distributed(rank, world, backend)
+    cname = os.environ.get("SWIFTLLM_CHANNEL", "/swiftllm-torchrun-" + os.environ.get("MASTER_PORT", "0"))
+    worker_loop(model_cfg, cfg, rank, world, local_rank, cname)
+
+
+class _Timer:
+    def __init__(self):
+        self.start = self.end = None
+        self.t0 = 0.0
+        self.ms = 0.0
+
+
+_TIMER = _Timer()
+
+
+def _timer_op(runner, op: str) -> float:
+    """Timed window over engine steps on every rank: barrier + synchronize on
+    both sides, CUDA events on the launching stream, max over ranks."""
+    import torch.distributed as dist
+    dev = runner.device
+    multi = dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1
+    if op == "start":
+        if runner.is_cuda:
+            torch.cuda.synchronize(dev)
+        if multi:
+            dist.barrier()
+        if runner.is_cuda:
+            torch.cuda.synchronize(dev)
+            _TIMER.start = torch.cuda.Event(enable_timing=True)
+            _TIMER.end = torch.cuda.Event(enable_timing=True)
+            _TIMER.start.record()
+        else:
+            _TIMER.t0 = time.perf_counter()
+        return 0.0
+    if op == "stop":
+        if runner.is_cuda:
+            _TIMER.end.record()
+            torch.cuda.synchronize(dev)
+            _TIMER.ms = _TIMER.start.elapsed_time(_TIMER.end)
+        else:
+            _TIMER.ms = (time.perf_counter() - _TIMER.t0) * 1e3
+        if multi:
+            dist.barrier()
+        return _TIMER.ms
+    if op == "report":
+        v = _TIMER.ms
+        if multi:
+            t = torch.tensor([v], dtype=torch.float64, device=dev if runner.is_cuda else "cpu")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+    raise ValueError(op)
 
 
 def _spawn_entry(rank, model_cfg, cfg, world, channel_name, port):
@@ -129,6 +195,12 @@ class LocalExecutor:
 
     def _backend(self) -> str:
         return "nccl" if self.cfg.device != "cpu" and torch.cuda.is_available() else "gloo"
+
+    def timer(self, op: str) -> float:
+        """Start / stop / report the device-timed window on every rank."""
+        if self.channel is not None:
+            self.channel.publish(pickle.dumps(("timer", op)), STEP_TIMEOUT)
+        return _timer_op(self.runner, op)
 
     def execute(self, si):
         if self.channel is not None:

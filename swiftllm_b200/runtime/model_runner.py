@@ -311,10 +311,12 @@ class ModelRunner:
                     self.model.compute_logits(h)
             torch.cuda.current_stream(dev).wait_stream(s)
             g = torch.cuda.CUDAGraph()
+            n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, pool=self.graph_pool):
                 h = self.model.forward(buf["ids"][:b], meta, self.kv_cache)
                 out = self.model.compute_logits(h)
-            self.graphs[b] = (g, {"out": out})
+            self.graphs[b] = (g, {"out": out, "launches": ops.LAUNCHES[0] - n0})
+            ops.LAUNCHES[0] = n0
         torch.cuda.synchronize(dev)
         log.info("captured %d decode graphs (max batch %d) in %.1fs", len(self.graphs), bmax,
                  time.time() - t0)
@@ -335,5 +337,6 @@ class ModelRunner:
             buf["seq_lens"][n:b].fill_(0)
         buf["bt"][:n, :MB].copy_(ints[o:o + n * MB].view(n, MB))
         g.replay()
+        ops.LAUNCHES[0] += io["launches"]
         self.stats["graph_steps"] += 1
         return io["out"][:n]

@@ -114,6 +114,8 @@ class BatchSampler:
             C.sample(tokens, lps, rows_logits, f.to(dev, non_blocking=True),
                      i.to(dev, non_blocking=True), k.to(dev, non_blocking=True),
                      bool(b.any_random))
+            from .. import ops as _ops
+            _ops._count()
             both = torch.stack([tokens.view(torch.float32), lps]).cpu().numpy()
             return both[0].view(np.int32).copy(), both[1].copy()
         lg = rows_logits.float().numpy()

@@ -1,0 +1,244 @@
+"""sm_100a kernels vs plain PyTorch fp32 references of the same ops.
+Shapes include odd tails, 1-token contexts and page-boundary contexts."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from swiftllm_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def C():
+    from swiftllm_b200.ops import cuda_ext
+    return cuda_ext()
+
+
+def _status_ok(C):
+    st = C.read_status(True)
+    assert st[0] == 0, f"device status word set: {st}"
+
+
+def bf(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda") * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("T,H", [(1, 256), (7, 4096), (33, 8192), (128, 5120), (5, 2560)])
+def test_rms_norm(C, T, H):
+    x, w = bf(T, H), bf(H)
+    out = torch.empty_like(x)
+    C.rms_norm(out, x, w, 1e-5)
+    r, _ = ref.rms_norm(x.float(), w.float(), 1e-5)
+    torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=2e-2)
+    res = bf(T, H)
+    res0 = res.clone()
+    out2 = torch.empty_like(x)
+    C.fused_add_rms_norm(out2, x, res, w, 1e-5)
+    r2, nr = ref.rms_norm(x, w, 1e-5, res0)
+    torch.testing.assert_close(res.float(), nr.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(out2.float(), r2.float(), rtol=2e-2, atol=3e-2)
+    _status_ok(C)
+
+
+def test_layer_norm(C):
+    x, w, b = bf(9, 2560), bf(2560), bf(2560)
+    out = torch.empty_like(x)
+    C.layer_norm(out, x, w, b, 1e-5)
+    r, _ = ref.layer_norm(x.float(), w.float(), b.float(), 1e-5)
+    torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=3e-2)
+
+
+def test_silu_gelu_embedding(C):
+    x = bf(37, 2 * 688)
+    out = torch.empty(37, 688, dtype=torch.bfloat16, device="cuda")
+    C.silu_and_mul(out, x)
+    torch.testing.assert_close(out.float(), ref.silu_and_mul(x.float()), rtol=2e-2, atol=2e-2)
+    g = torch.empty_like(x)
+    C.gelu_tanh(g, x)
+    torch.testing.assert_close(g.float(), ref.gelu_tanh(x.float()), rtol=2e-2, atol=2e-2)
+    w = bf(1000, 256)
+    ids = torch.tensor([0, 5, 999, 1000, 3], dtype=torch.int32, device="cuda")
+    e = torch.empty(5, 256, dtype=torch.bfloat16, device="cuda")
+    C.embedding(e, ids, w, 0)
+    assert torch.equal(e[:3], w[[0, 5, 999]]) and e[3].abs().sum() == 0
+    e2 = torch.empty_like(e)
+    C.embedding(e2, ids, w[500:].contiguous(), 500)
+    assert torch.equal(e2[2], w[999]) and e2[0].abs().sum() == 0
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,rot,bias", [(4, 2, 64, 64, False), (32, 8, 128, 128, True),
+                                                (8, 8, 80, 32, True)])
+def test_qkv_rope_cache(C, Hq, Hkv, D, rot, bias):
+    from swiftllm_b200.models.rope import cos_sin_table
+    T, L, bs, nb = 37, 3, 16, 8
+    qkv = bf(T, (Hq + 2 * Hkv) * D)
+    b = bf((Hq + 2 * Hkv) * D) if bias else None
+    pos = torch.randint(0, 500, (T,), dtype=torch.int32, device="cuda")
+    slots = torch.randperm(nb * bs, device="cuda")[:T].to(torch.int32)
+    slots[3] = -1
+    cs = cos_sin_table(rot, 10000.0, 512, device="cuda")
+    kv = torch.zeros(nb, L, 2, Hkv, bs, D, dtype=torch.bfloat16, device="cuda")
+    kv_ref = kv.clone()
+    q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device="cuda")
+    C.qkv_rope_cache(q, qkv, pos, cs, kv, 1, slots, Hq, Hkv, D, rot, b)
+    x = qkv.float() + (b.float() if b is not None else 0)
+    qr = ref.apply_rope(x[:, :Hq * D].view(T, Hq, D), pos, cs, rot)
+    kr = ref.apply_rope(x[:, Hq * D:(Hq + Hkv) * D].reshape(T, Hkv, D), pos, cs, rot)
+    vr = x[:, (Hq + Hkv) * D:].reshape(T, Hkv, D)
+    ref.write_kv(kv_ref[:, 1, 0], kv_ref[:, 1, 1], kr, vr, slots)
+    torch.testing.assert_close(q.float(), qr, rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(kv.float(), kv_ref.float(), rtol=2e-2, atol=2e-2)
+    _status_ok(C)
+
+
+def _paged_setup(lens, q_lens, Hq, Hkv, D, bs=16, L=2):
+    S = len(lens)
+    nbs = [(l + bs - 1) // bs for l in lens]
+    total = sum(nbs) + 3
+    kv = bf(total, L, 2, Hkv, bs, D)
+    perm = torch.randperm(total, device="cuda").to(torch.int32)
+    mb = max(max(nbs), 1)
+    bt = torch.zeros((S, mb + 2), dtype=torch.int32, device="cuda")
+    o = 0
+    for i, n in enumerate(nbs):
+        bt[i, :n] = perm[o:o + n]
+        o += n
+    q_start = torch.tensor(np.concatenate([[0], np.cumsum(q_lens)]), dtype=torch.int32, device="cuda")
+    q = bf(int(sum(q_lens)), Hq, D)
+    sl = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    return kv, bt, q_start, q, sl
+
+
+def _ref_attn(q, kv, bt, q_start, sl, scale, window=None):
+    return ref.paged_attention(q.float().cpu(), kv[:, 1, 0].float().cpu(), kv[:, 1, 1].float().cpu(),
+                               bt.cpu(), q_start.cpu(), sl.cpu(), scale, sliding_window=window)
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,bs", [(32, 32, 128, 16), (32, 8, 128, 16), (8, 1, 128, 16),
+                                         (4, 2, 64, 16), (32, 32, 80, 16), (8, 8, 128, 32)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_decode(C, Hq, Hkv, D, bs, splits):
+    lens = [1, 15, 16, 17, 200, 1000, 0, 33]
+    kv, bt, q_start, q, sl = _paged_setup(lens, [1] * len(lens), Hq, Hkv, D, bs)
+    rows = len(lens)
+    ws = torch.empty(rows * Hq * splits * (D + 2), dtype=torch.float32, device="cuda")
+    out = torch.empty_like(q)
+    scale = 1 / math.sqrt(D)
+    C.paged_decode(out, q, kv, 1, bt, sl, rows, splits, scale, 0, ws)
+    r = _ref_attn(q, kv, bt, q_start, sl, scale)
+    for i, l in enumerate(lens):
+        if l == 0:
+            assert out[i].float().abs().max() == 0
+            continue
+        torch.testing.assert_close(out[i].float().cpu(), r[i], rtol=2e-2, atol=2e-2)
+    _status_ok(C)
+
+
+def test_paged_decode_window(C):
+    lens = [100, 300, 17]
+    kv, bt, q_start, q, sl = _paged_setup(lens, [1] * 3, 8, 2, 128)
+    ws = torch.empty(3 * 8 * 2 * 130, dtype=torch.float32, device="cuda")
+    out = torch.empty_like(q)
+    C.paged_decode(out, q, kv, 1, bt, sl, 3, 2, 0.088, 64, ws)
+    r = _ref_attn(q, kv, bt, q_start, sl, 0.088, 64)
+    torch.testing.assert_close(out.float().cpu(), r, rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(32, 32, 128), (32, 8, 128), (4, 2, 64), (8, 8, 80)])
+def test_paged_prefill(C, Hq, Hkv, D):
+    # (seq_len, q_len): full prompts, chunked prefill with cached prefix, odd tails
+    pairs = [(64, 64), (130, 130), (300, 45), (17, 17), (1, 1), (200, 129)]
+    lens = [p[0] for p in pairs]
+    ql = [p[1] for p in pairs]
+    kv, bt, q_start, q, sl = _paged_setup(lens, ql, Hq, Hkv, D)
+    scale = 1 / math.sqrt(D)
+    out = torch.zeros_like(q)
+    C.paged_prefill(out, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 0)
+    torch.testing.assert_close(out.float().cpu(), _ref_attn(q, kv, bt, q_start, sl, scale),
+                               rtol=2e-2, atol=2e-2)
+    out2 = torch.zeros_like(q)
+    C.paged_prefill(out2, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 50)
+    torch.testing.assert_close(out2.float().cpu(), _ref_attn(q, kv, bt, q_start, sl, scale, 50),
+                               rtol=2e-2, atol=2e-2)
+    _status_ok(C)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (7, 12288, 4096), (16, 128, 64),
+                                   (33, 4096, 11008), (256, 4096, 4096), (256, 22016, 4096),
+                                   (1000, 4096, 4096), (4096, 1024, 512), (77, 32000, 4096),
+                                   (300, 640, 200)])
+def test_gemm(C, T, N, K):
+    x = bf(T, K, scale=0.5)
+    w = bf(N, K, scale=0.05)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+    C.gemm(out, x, w, None)
+    r = x.float() @ w.float().t()
+    torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=2e-2 * math.sqrt(K / 64) * 0.5)
+    _status_ok(C)
+
+
+def test_gemm_bias_and_strided_out(C):
+    x, w, b = bf(40, 512), bf(384, 512, scale=0.05), bf(384)
+    big = torch.zeros(40, 1024, dtype=torch.bfloat16, device="cuda")
+    out = big[:, 128:512]
+    C.gemm(out, x, w, b)
+    r = x.float() @ w.float().t() + b.float()
+    torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=5e-2)
+    assert big[:, :128].abs().sum() == 0 and big[:, 512:].abs().sum() == 0
+
+
+def test_sample_greedy_and_seeded(C):
+    from swiftllm_b200 import _core
+    from swiftllm_b200.parallel.dummy_init import mix_key
+    n, V = 64, 32000
+    logits = torch.randn(n, V, device="cuda") * 3
+    idx = np.arange(n)
+    temp = np.where(idx % 4 == 0, 0.0, 0.8).astype(np.float32)
+    top_p = np.where(idx % 3 == 0, 0.9, 1.0).astype(np.float32)
+    top_k = np.where(idx % 5 == 0, 50, -1).astype(np.int32)
+    min_p = np.where(idx % 7 == 0, 0.05, 0.0).astype(np.float32)
+    key = mix_key(1234, 0x5EED)
+    c0 = np.arange(n, dtype=np.uint32)
+    f = torch.from_numpy(np.stack([temp, top_p, min_p])).cuda()
+    i = torch.from_numpy(np.stack([idx.astype(np.int32), top_k, c0.view(np.int32),
+                                   np.zeros(n, np.int32)])).cuda()
+    keys = torch.full((n,), int(np.uint64(key).view(np.int64)), dtype=torch.int64, device="cuda")
+    toks = torch.empty(n, dtype=torch.int32, device="cuda")
+    lps = torch.empty(n, dtype=torch.float32, device="cuda")
+    C.sample(toks, lps, logits, f, i, keys, True)
+    toks, lps = toks.cpu().numpy(), lps.cpu().numpy()
+    lg = logits.cpu().numpy()
+    mism = 0
+    for r in range(n):
+        u = _core.philox_uniform(key, int(c0[r]), 0)
+        p = _core.SampleParams(temperature=float(temp[r]), top_p=float(top_p[r]),
+                               top_k=int(top_k[r]), min_p=float(min_p[r]))
+        t, lp = _core.sample_row(lg[r], p, u)
+        if t != toks[r]:
+            mism += 1
+        else:
+            assert abs(lp - lps[r]) < 1e-3
+        if temp[r] == 0:
+            assert toks[r] == int(np.argmax(lg[r]))
+    assert mism <= 2, f"{mism} of {n} draws differ from the CPU oracle"
+
+
+def test_copy_blocks_and_init(C):
+    kv = bf(10, 2, 2, 2, 16, 64)
+    ref_kv = kv.clone()
+    pairs = torch.tensor([[1, 5], [3, 7]], dtype=torch.int32, device="cuda")
+    C.copy_blocks(kv, pairs)
+    ref_kv[5] = ref_kv[1]
+    ref_kv[7] = ref_kv[3]
+    assert torch.equal(kv, ref_kv)
+    from swiftllm_b200.parallel.dummy_init import fill_normal_sharded
+    g = torch.empty(64, 96, dtype=torch.float32, device="cuda")
+    c = torch.empty(64, 96, dtype=torch.float32)
+    fill_normal_sharded(g, None, 0, 7, 0.02)
+    fill_normal_sharded(c, None, 0, 7, 0.02)
+    torch.testing.assert_close(g.cpu(), c, rtol=1e-4, atol=1e-6)
+    assert abs(float(g.std()) - 0.02) < 0.003
