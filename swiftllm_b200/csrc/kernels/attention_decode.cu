@@ -325,3 +325,97 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
 }
 
 }  // namespace swift
+
+// ---------------------------------------------------------------------------
+// Allocation-free C entry point (declared in swift_noalloc.h; no counterpart
+// in the reference). The split-KV scratch that paged_decode takes from the
+// caller lives here in a fixed device array instead.
+#include "swift_noalloc.h"
+
+static __device__ __align__(256) float g_noalloc_scratch[SWIFT_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace swift {
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+float* g_noalloc_ptr[kNoallocMaxDevices] = {nullptr};
+
+// Once per device, with that device current: the device address of the
+// scratch array (host code must not use the array's name as a pointer).
+int noalloc_setup(float** scratch) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  if (dev < 0 || dev >= kNoallocMaxDevices) return SWIFT_NOALLOC_ERR_CUDA;
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
+      return SWIFT_NOALLOC_ERR_CUDA;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *scratch = g_noalloc_ptr[dev];
+  return SWIFT_NOALLOC_OK;
+}
+
+template <int D, int BS>
+int noalloc_decode(void* out, const void* q, const void* kv, int64_t blk_stride, int64_t layer_off,
+                   int64_t kv_stride, const int32_t* bt, int64_t bt_stride,
+                   const int32_t* seq_lens, int rows, int Hq, int Hkv, int splits, float scale,
+                   int window, float* scratch, cudaStream_t stream) {
+  using C = DecodeCfg<D, BS>;
+  auto kern = paged_decode_kernel<D, BS>;
+  static bool attr_set[kNoallocMaxDevices] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::SMEM)) != cudaSuccess)
+      return SWIFT_NOALLOC_ERR_CUDA;
+    attr_set[dev] = true;
+  }
+  dim3 grid(rows, Hkv, splits);
+  kern<<<grid, kDecWarps * 32, C::SMEM, stream>>>(
+      static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
+      static_cast<const __nv_bfloat16*>(kv), blk_stride, layer_off, kv_stride, bt, bt_stride,
+      seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  if (splits > 1) {
+    decode_combine_kernel<D><<<dim3(rows, Hq), 128, 0, stream>>>(
+        static_cast<__nv_bfloat16*>(out), scratch, rows, Hq, splits);
+    if (cudaGetLastError() != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  }
+  return SWIFT_NOALLOC_OK;
+}
+
+}  // namespace
+}  // namespace swift
+
+extern "C" __attribute__((visibility("default"))) int swift_paged_decode_noalloc(
+    void* out, const void* q, const void* kv, int64_t blk_stride, int64_t layer_off,
+    int64_t kv_stride, int block_size, int head_dim, const int32_t* bt, int64_t bt_stride,
+    const int32_t* seq_lens, int rows, int Hq, int Hkv, int splits, float scale, int window,
+    cudaStream_t stream) {
+  using namespace swift;
+  if (!out || !q || !kv || !bt || !seq_lens || rows <= 0 || Hq <= 0 || Hkv <= 0 || splits <= 0)
+    return SWIFT_NOALLOC_ERR_ARGS;
+  if (Hq % Hkv != 0 || Hq / Hkv > kMaxGroup) return SWIFT_NOALLOC_ERR_UNSUPPORTED;
+  const uint64_t need = splits > 1
+      ? static_cast<uint64_t>(rows) * Hq * splits * (static_cast<uint64_t>(head_dim) + 2) * sizeof(float)
+      : 0;
+  if (need > SWIFT_NOALLOC_SCRATCH_BYTES) return SWIFT_NOALLOC_ERR_TOO_LARGE;
+  float* scratch = nullptr;
+  int st = noalloc_setup(&scratch);
+  if (st != SWIFT_NOALLOC_OK) return st;
+#define NOALLOC_CASE(d, bs)                                                                     \
+  if (head_dim == d && block_size == bs)                                                        \
+    return noalloc_decode<d, bs>(out, q, kv, blk_stride, layer_off, kv_stride, bt, bt_stride,   \
+                                 seq_lens, rows, Hq, Hkv, splits, scale, window, scratch, stream);
+  NOALLOC_CASE(128, 16)
+  NOALLOC_CASE(128, 32)
+  NOALLOC_CASE(128, 8)
+  NOALLOC_CASE(64, 16)
+  NOALLOC_CASE(64, 32)
+  NOALLOC_CASE(80, 16)
+  NOALLOC_CASE(96, 16)
+#undef NOALLOC_CASE
+  return SWIFT_NOALLOC_ERR_UNSUPPORTED;
+}
