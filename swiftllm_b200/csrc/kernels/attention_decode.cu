@@ -23,7 +23,7 @@
 namespace swift {
 
 constexpr int kDecWarps = 4;
-constexpr int kDecStages = 4;
+constexpr int kDecStages = 2;
 constexpr int kMaxGroup = 8;
 
 template <int D, int BS>
@@ -32,17 +32,23 @@ struct DecodeCfg {
   static constexpr int DL = D / LPT;             // channels per lane in QK
   static constexpr int CH = DL * 2 / 16;         // 16-byte chunks per lane in QK
   static constexpr int DP = (D + 31) / 32;       // channels per lane in PV
+  // PV channel ownership: contiguous (lane*DP + d, bf16x2 loads) when DP is
+  // even, else strided (lane + 32*d)
+  static constexpr bool CONTIG = (D % 64) == 0;
   static constexpr int PAGE = BS * D * 2;        // bytes of one (layer, k|v, head) page
   static constexpr int STAGE = 2 * PAGE;
-  static constexpr int NST = STAGE >= 16384 ? 2 : kDecStages;  // ring depth per warp
-  static constexpr size_t SMEM = size_t(kDecWarps) * NST * STAGE + kMaxGroup * D * 4 +
-                                 size_t(kDecWarps) * kMaxGroup * (D + 2) * 4 +
-                                 kDecWarps * NST * 8 + 16;
+  static constexpr int NST = STAGE >= 16384 ? 1 : kDecStages;  // ring depth per warp
+  static constexpr size_t RING = size_t(kDecWarps) * NST * STAGE;
+  // shared bytes for GQA group g: ring + q + per-warp merge buffers + barriers
+  static constexpr size_t smem_for(int g) {
+    return RING + size_t(g) * D * 4 + size_t(kDecWarps) * g * (D + 2) * 4 + kDecWarps * NST * 8 + 16;
+  }
+  static constexpr size_t SMEM = smem_for(kMaxGroup);
   static_assert((DL * 2) % 16 == 0, "QK lane slice must be whole 16-byte chunks");
 };
 
 template <int D, int BS>
-__global__ void __launch_bounds__(kDecWarps * 32)
+__global__ void __launch_bounds__(kDecWarps * 32, 3)
     paged_decode_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ q,
                         const __nv_bfloat16* __restrict__ kv, int64_t blk_stride,
                         int64_t layer_off, int64_t kv_stride, const int32_t* __restrict__ bt,
@@ -52,12 +58,12 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   using C = DecodeCfg<D, BS>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  float* q_s = reinterpret_cast<float*>(smem + size_t(kDecWarps) * C::NST * C::STAGE);
-  float* merge = q_s + kMaxGroup * D;  // [warps][G][D] acc, then [warps][G][2] (m, l)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + kDecWarps * kMaxGroup * (D + 2));
+  const int G = Hq / Hkv;
+  float* q_s = reinterpret_cast<float*>(smem + C::RING);
+  float* merge = q_s + G * D;  // [warps][G][D] acc, then [warps][G][2] (m, l)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge + kDecWarps * G * (D + 2));
 
   const int row = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
-  const int G = Hq / Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int len = seq_lens[row];
 
@@ -158,10 +164,20 @@ __global__ void __launch_bounds__(kDecWarps * 32)
 #pragma unroll 4
     for (int t = 0; t < BS; ++t) {
       float vf[C::DP];
+      if constexpr (C::CONTIG) {
 #pragma unroll
-      for (int d = 0; d < C::DP; ++d) {
-        int ch = lane + 32 * d;
-        vf[d] = ch < D ? __bfloat162float(vs[t * D + ch]) : 0.f;
+        for (int d = 0; d < C::DP; d += 2) {
+          float2 f2 = __bfloat1622float2(
+              *reinterpret_cast<const __nv_bfloat162*>(vs + t * D + lane * C::DP + d));
+          vf[d] = f2.x;
+          vf[d + 1] = f2.y;
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < C::DP; ++d) {
+          int ch = lane + 32 * d;
+          vf[d] = ch < D ? __bfloat162float(vs[t * D + ch]) : 0.f;
+        }
       }
 #pragma unroll
       for (int g = 0; g < kMaxGroup; ++g) {
@@ -184,18 +200,18 @@ __global__ void __launch_bounds__(kDecWarps * 32)
   }
 
   float* macc = merge;                             // [W][G][D]
-  float* mml = merge + kDecWarps * kMaxGroup * D;  // [W][G][2]
+  float* mml = merge + kDecWarps * G * D;  // [W][G][2]
 #pragma unroll
   for (int g = 0; g < kMaxGroup; ++g) {
     if (g < G) {
 #pragma unroll
       for (int d = 0; d < C::DP; ++d) {
-        int ch = lane + 32 * d;
-        if (ch < D) macc[(warp * kMaxGroup + g) * D + ch] = acc[g][d];
+        int ch = C::CONTIG ? lane * C::DP + d : lane + 32 * d;
+        if (ch < D) macc[(warp * G + g) * D + ch] = acc[g][d];
       }
       if (lane == 0) {
-        mml[(warp * kMaxGroup + g) * 2] = m[g];
-        mml[(warp * kMaxGroup + g) * 2 + 1] = l[g];
+        mml[(warp * G + g) * 2] = m[g];
+        mml[(warp * G + g) * 2 + 1] = l[g];
       }
     }
   }
@@ -204,16 +220,16 @@ __global__ void __launch_bounds__(kDecWarps * 32)
     int g = i / D, ch = i % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, mml[(w * kMaxGroup + g) * 2]);
+    for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, mml[(w * G + g) * 2]);
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kDecWarps; ++w) {
-        float mw = mml[(w * kMaxGroup + g) * 2];
+        float mw = mml[(w * G + g) * 2];
         if (mw == -INFINITY) continue;
         float f = __expf(mw - M);
-        L += mml[(w * kMaxGroup + g) * 2 + 1] * f;
-        O += macc[(w * kMaxGroup + g) * D + ch] * f;
+        L += mml[(w * G + g) * 2 + 1] * f;
+        O += macc[(w * G + g) * D + ch] * f;
       }
     }
     const int h = kvh * G + g;
@@ -275,7 +291,7 @@ static void launch_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, 
     TORCH_CHECK(ws.numel() >= int64_t(rows) * Hq * splits * (D + 2), "decode workspace too small");
   dim3 grid(rows, Hkv, splits);
   auto st = cur_stream();
-  kern<<<grid, kDecWarps * 32, C::SMEM, st>>>(
+  kern<<<grid, kDecWarps * 32, C::smem_for(Hq / Hkv), st>>>(
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(kv.data_ptr<at::BFloat16>()), kv.stride(0),
@@ -373,7 +389,7 @@ int noalloc_decode(void* out, const void* q, const void* kv, int64_t blk_stride,
     attr_set[dev] = true;
   }
   dim3 grid(rows, Hkv, splits);
-  kern<<<grid, kDecWarps * 32, C::SMEM, stream>>>(
+  kern<<<grid, kDecWarps * 32, C::smem_for(Hq / Hkv), stream>>>(
       static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
       static_cast<const __nv_bfloat16*>(kv), blk_stride, layer_off, kv_stride, bt, bt_stride,
       seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, nullptr);
