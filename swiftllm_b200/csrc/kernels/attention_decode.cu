@@ -22,6 +22,11 @@
 
 namespace swift {
 
+// attention_decode_tc.cu: tensor-core kernel for block size 16, head_dim 64/128
+bool paged_decode_tc(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
+                     torch::Tensor bt, torch::Tensor seq_lens, int rows, int splits, double scale,
+                     int window, torch::Tensor ws);
+
 constexpr int kDecWarps = 4;
 constexpr int kDecStages = 2;
 constexpr int kMaxGroup = 8;
@@ -322,6 +327,23 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
   if (rows <= 0) return 0;
   const int D = static_cast<int>(q.size(2)), BS = static_cast<int>(kv.size(4));
   splits = std::max<int64_t>(1, splits);
+  if (splits > 1)
+    TORCH_CHECK(ws.numel() >= rows * q.size(1) * splits * (D + 2), "decode workspace too small");
+  // tensor-core path (block size 16, head_dim 64 / 128)
+  if (paged_decode_tc(out, q, kv, layer, bt, seq_lens, static_cast<int>(rows),
+                      static_cast<int>(splits), scale, static_cast<int>(window), ws)) {
+    if (splits == 1) return 1;
+    const int Hq = static_cast<int>(q.size(1));
+    auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+    if (D == 128)
+      decode_combine_kernel<128><<<dim3(rows, Hq), 128, 0, cur_stream()>>>(
+          op, ws.data_ptr<float>(), static_cast<int>(rows), Hq, static_cast<int>(splits));
+    else
+      decode_combine_kernel<64><<<dim3(rows, Hq), 128, 0, cur_stream()>>>(
+          op, ws.data_ptr<float>(), static_cast<int>(rows), Hq, static_cast<int>(splits));
+    SWIFT_CHECK_LAUNCH();
+    return 2;
+  }
 #define DEC_CASE(d, bs)                                                                  \
   if (D == d && BS == bs) {                                                              \
     launch_decode<d, bs>(out, q, kv, layer, bt, seq_lens, static_cast<int>(rows),         \
