@@ -12,7 +12,7 @@
 //
 // Structure (one CTA of 6 warps per SM, persistent over output tiles):
 //   warp 0      TMA producer: cp.async.bulk.tensor 2-D loads (128B swizzle,
-//               no multicast) of a 128x64 weight tile and a BNx64 token tile
+//               plain per-CTA loads) of a 128x64 weight tile and a BNx64 token tile
 //               per stage into an STAGES-deep shared-memory ring;
 //   warp 1      allocates TMEM; one thread issues
 //               tcgen05.mma.cta_group::1.kind::f16 (bf16 in, fp32 in TMEM);

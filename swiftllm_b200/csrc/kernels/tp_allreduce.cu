@@ -1,0 +1,170 @@
+// Tensor-parallel sum of the row-parallel GEMM outputs over NVLink peer memory.
+//
+// The reference declares TP all-reduce and returns NotImplemented
+// (crates/swiftllm-core/src/execution/tensor_parallel.rs:115-141).
+//
+// Memory: one symmetric allocation per rank (same layout on every GPU, every
+// rank holds the device addresses of all peers' copies, rendezvoused through
+// torch.distributed._symmetric_memory):
+//   [flags | in A | in B | red A | red B]
+// The o_proj / down_proj GEMM epilogue stores its partial output directly in
+// this rank's `in` buffer (A/B alternate by call so consecutive calls need no
+// exit barrier), then this kernel runs a two-shot reduction:
+//   phase 1  (reduce-scatter) block b sums, in fixed rank order and fp32, the
+//            elements of this rank's 1/k slice that block b owns, loading
+//            every peer's `in` over NVLink, and stores bf16 to its `red`;
+//   phase 2  (all-gather) block b reads the elements that block b of each
+//            peer produced in phase 1 from that peer's `red` into `out`.
+// Each phase starts with a per-block barrier: block b stores the call epoch
+// into every peer's flag slot for (phase, b, this rank) with st.release.sys
+// and polls its own slots with ld.acquire.sys. Because every rank uses the
+// same grid and the same element-to-block mapping, block b only ever waits
+// for block b of its peers. Epochs live in device memory and advance inside
+// the kernel, so CUDA-graph replays keep counting. Every poll is bounded by
+// a %globaltimer deadline; on expiry the block records kErrPeerTimeout in the
+// status word and returns (the host raises CommTimeoutError).
+#include "common.cuh"
+
+namespace swift {
+
+constexpr int kArMaxRanks = 8;
+constexpr int kArBlocks = 64;
+constexpr int kArThreads = 512;
+
+struct ArPeers {
+  uint64_t base[kArMaxRanks];  // byte address of each rank's symmetric allocation
+};
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// flags: [2 phases][kArBlocks][kArMaxRanks] uint32 at offset 0 of each allocation.
+__device__ __forceinline__ bool block_barrier(const ArPeers& P, int rank, int k, int phase,
+                                              uint32_t epoch, int64_t timeout_ns, int* status) {
+  __syncthreads();
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  const int t = threadIdx.x;
+  if (t < k) {
+    const int slot = (phase * kArBlocks + blockIdx.x) * kArMaxRanks;
+    // announce: my arrival in peer t's slot [.., rank]
+    uint32_t* remote = reinterpret_cast<uint32_t*>(P.base[t]) + slot + rank;
+    __threadfence_system();
+    st_release_sys(remote, epoch);
+    // wait: peer t's arrival in my slot [.., t]
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(P.base[rank]) + slot + t;
+    const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(timeout_ns);
+    while (static_cast<int32_t>(ld_acquire_sys(mine) - epoch) < 0) {
+      if (globaltimer_ns() > deadline) {
+        set_status(status, kErrPeerTimeout, 200 + phase);
+        atomicExch(&ok, 0);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__global__ void __launch_bounds__(kArThreads)
+    tp_allreduce_kernel(ArPeers P, int rank, int k, int64_t in_off, int64_t red_off,
+                        __nv_bfloat16* __restrict__ out, int64_t n, uint32_t* __restrict__ epochs,
+                        int64_t timeout_ns, int* status) {
+  const uint32_t epoch = epochs[blockIdx.x] + 1;
+  // slice boundaries in units of 8 elements (16-byte vectors)
+  const int64_t nv = n / 8;
+  auto slice_lo = [&](int r) { return nv * r / k; };
+  if (!block_barrier(P, rank, k, 0, epoch, timeout_ns, status)) return;
+  {
+    const int64_t lo = slice_lo(rank), hi = slice_lo(rank + 1);
+    uint4* red = reinterpret_cast<uint4*>(P.base[rank] + red_off);
+    for (int64_t v = lo + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < hi;
+         v += int64_t(gridDim.x) * blockDim.x) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int r = 0; r < k; ++r) {
+        const uint4* src = reinterpret_cast<const uint4*>(P.base[r] + in_off) + v;
+        uint4 x = __ldcg(src);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(h[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+      red[v] = o;
+    }
+  }
+  if (!block_barrier(P, rank, k, 1, epoch, timeout_ns, status)) return;
+  for (int r = 0; r < k; ++r) {
+    const int64_t lo = slice_lo(r), hi = slice_lo(r + 1);
+    const uint4* src = reinterpret_cast<const uint4*>(P.base[r] + red_off);
+    uint4* dst = reinterpret_cast<uint4*>(out);
+    for (int64_t v = lo + blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < hi;
+         v += int64_t(gridDim.x) * blockDim.x)
+      dst[v] = __ldcg(src + v);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) epochs[blockIdx.x] = epoch;
+}
+
+// out [n] bf16 (local); bases: int64 [k] byte addresses of the symmetric
+// allocations; in_off / red_off: byte offsets of this call's buffers.
+void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
+                  int64_t red_off, torch::Tensor epochs, double timeout_s) {
+  CHECK_BF16(out);
+  CHECK_CONTIG(out);
+  const int k = static_cast<int>(bases.size());
+  TORCH_CHECK(k >= 1 && k <= kArMaxRanks);
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= kArBlocks);
+  const int64_t n = out.numel();
+  TORCH_CHECK(n % 8 == 0, "all-reduce size must be a multiple of 8 elements");
+  TORCH_CHECK(in_off % 16 == 0 && red_off % 16 == 0);
+  ArPeers P;
+  for (int r = 0; r < kArMaxRanks; ++r) P.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
+  tp_allreduce_kernel<<<kArBlocks, kArThreads, 0, cur_stream()>>>(
+      P, static_cast<int>(rank), k, in_off, red_off,
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), n,
+      reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>()),
+      static_cast<int64_t>(timeout_s * 1e9), status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+}
+
+// Test hook: one bounded wait on a flag nobody sets (single GPU, no peer):
+// must return with kErrPeerTimeout recorded, the context still usable.
+__global__ void flag_wait_probe_kernel(const uint32_t* flag, uint32_t want, int64_t timeout_ns,
+                                       int* status) {
+  const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(timeout_ns);
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - want) < 0) {
+    if (globaltimer_ns() > deadline) {
+      set_status(status, kErrPeerTimeout, 299);
+      return;
+    }
+  }
+}
+
+void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s) {
+  TORCH_CHECK(flag.scalar_type() == at::kInt && flag.is_cuda());
+  flag_wait_probe_kernel<<<1, 1, 0, cur_stream()>>>(
+      reinterpret_cast<const uint32_t*>(flag.data_ptr<int32_t>()), static_cast<uint32_t>(want),
+      static_cast<int64_t>(timeout_s * 1e9), status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+}
+
+}  // namespace swift

@@ -240,8 +240,16 @@ class DecoderModel:
                                self.local_heads, self.local_kv_heads, c.head_dim, c.rotary_dim,
                                L.bqkv)
         a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
-        o = ops.linear(a.reshape(a.shape[0], -1), L.wo)
-        return o
+        return ops.linear(a.reshape(a.shape[0], -1), L.wo,
+                          out=self._reduce_slot(a.shape[0]))
+
+    def _reduce_slot(self, T: int):
+        """Where a row-parallel GEMM should write its partial output: the
+        fused TP backend hands out its NVLink-visible buffer (GEMM -> reduce
+        with no copy); otherwise None (a fresh tensor)."""
+        if self.tp.size > 1 and self.device.type == "cuda" and hasattr(self.tp, "reduce_buffer"):
+            return self.tp.reduce_buffer(T, self.cfg.hidden_size)
+        return None
 
     def _mlp(self, L, x: torch.Tensor) -> torch.Tensor:
         c = self.cfg
@@ -254,7 +262,7 @@ class DecoderModel:
             return ops.linear(h, L.w2)
         h = ops.linear(x, L.w13)
         h = ops.silu_and_mul(h)
-        return ops.linear(h, L.w2)
+        return ops.linear(h, L.w2, out=self._reduce_slot(h.shape[0]))
 
     def forward(self, input_ids: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor) -> torch.Tensor:
         """Returns final hidden states of the rows in ``meta.logits_idx``."""

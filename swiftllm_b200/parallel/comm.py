@@ -63,10 +63,10 @@ class NcclTP(TPGroup):
 
 
 def build_tp_group(rank: int, world: int, device: torch.device, backend: str,
-                   model_cfg=None) -> TPGroup:
+                   model_cfg=None, max_tokens: int = 8192) -> TPGroup:
     if world == 1:
         return TPGroup(0, 1)
     if backend == "fused" and device.type == "cuda":
         from .fused_comm import FusedTP
-        return FusedTP(rank, world, device, model_cfg)
+        return FusedTP(rank, world, device, model_cfg, max_tokens)
     return NcclTP(rank, world)

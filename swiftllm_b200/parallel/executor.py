@@ -44,7 +44,8 @@ def _device_for(cfg, local_rank: int) -> torch.device:
 def _build_runner(model_cfg, cfg, rank: int, world: int, local_rank: int):
     from ..runtime.model_runner import ModelRunner
     device = _device_for(cfg, local_rank)
-    tp = build_tp_group(rank, world, device, cfg.comm_backend, model_cfg)
+    tp = build_tp_group(rank, world, device, cfg.comm_backend, model_cfg,
+                        max(int(cfg.max_num_batched_tokens or 8192), 16384))
     if cfg.comm_backend == "nccl" and device.type == "cuda":
         from .. import ops
         ops.set_gemm_backend("cublas")

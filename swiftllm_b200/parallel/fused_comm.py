@@ -1,0 +1,89 @@
+"""Fused tensor-parallel reduction over NVLink peer memory (the product
+backend; NCCL is the baseline).
+
+The row-parallel GEMMs (o_proj, down_proj) write their partial sums straight
+into this rank's slot of a symmetric allocation (``reduce_buffer``); the
+reduction kernel (csrc/kernels/tp_allreduce.cu) then sums all ranks'
+partials with peer loads and per-block release/acquire flags, so no NCCL
+call sits on the per-layer path. The vocab-parallel logits gather stays on
+NCCL (one small call per step).
+
+Layout of the symmetric allocation (bytes):
+  [flags 64 KiB | in A | in B | red A | red B], each buffer max_tokens x H bf16.
+"""
+
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+
+from ..utils.logging import get_logger
+from .comm import NcclTP
+from .failures import CommTimeoutError
+
+log = get_logger(__name__)
+
+_FLAGS_BYTES = 64 << 10
+TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
+
+
+class FusedTP(NcclTP):
+    def __init__(self, rank: int, size: int, device: torch.device, model_cfg,
+                 max_tokens: int = 8192):
+        super().__init__(rank, size)
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from ..ops import cuda_ext
+        self.C = cuda_ext()
+        self.device = device
+        H = model_cfg.hidden_size
+        self.max_elems = max_tokens * H
+        self.buf_bytes = (self.max_elems * 2 + 255) // 256 * 256
+        total = _FLAGS_BYTES + 4 * self.buf_bytes
+        self.symm = symm_mem.empty(total // 2, dtype=torch.bfloat16, device=device)
+        self.symm.zero_()
+        torch.cuda.synchronize(device)
+        self.hdl = symm_mem.rendezvous(self.symm, dist.group.WORLD)
+        self.bases = [int(p) for p in self.hdl.buffer_ptrs]
+        assert len(self.bases) == size
+        self.epochs = torch.zeros(64, dtype=torch.int32, device=device)
+        self.call = 0
+        dist.barrier()
+        log.info("fused TP comm ready: rank %d/%d, %.1f MiB symmetric", rank, size,
+                 total / 2**20)
+
+    def _off(self, kind: str, parity: int) -> int:
+        base = _FLAGS_BYTES + (0 if kind == "in" else 2 * self.buf_bytes)
+        return base + parity * self.buf_bytes
+
+    def reduce_buffer(self, T: int, H: int) -> Optional[torch.Tensor]:
+        """This rank's input slot for the next reduce: the producing GEMM
+        stores its partial output here."""
+        n = T * H
+        if n > self.max_elems:
+            return None
+        off = self._off("in", self.call % 2) // 2
+        return self.symm[off:off + n].view(T, H)
+
+    def reduce(self, x: torch.Tensor) -> torch.Tensor:
+        n = x.numel()
+        if n > self.max_elems or n % 8:
+            return super().reduce(x)
+        parity = self.call % 2
+        slot = self.reduce_buffer(x.shape[0], n // x.shape[0])
+        if x.data_ptr() != slot.data_ptr():
+            slot.copy_(x.view_as(slot))
+        out = torch.empty_like(x)
+        self.C.tp_allreduce(out, self.bases, self.rank, self._off("in", parity),
+                            self._off("red", parity), self.epochs, TIMEOUT_S)
+        from .. import ops
+        ops._count()
+        self.call += 1
+        return out
+
+    def check(self) -> None:
+        st = self.C.read_status(True)
+        if st[0] == 2:
+            raise CommTimeoutError(f"peer did not arrive within {TIMEOUT_S}s (site {st[1]})")

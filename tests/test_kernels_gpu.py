@@ -242,3 +242,18 @@ def test_copy_blocks_and_init(C):
     fill_normal_sharded(c, None, 0, 7, 0.02)
     torch.testing.assert_close(g.cpu(), c, rtol=1e-4, atol=1e-6)
     assert abs(float(g.std()) - 0.02) < 0.003
+
+
+def test_peer_wait_times_out_cleanly(C):
+    # a flag nobody sets: the bounded wait must give up, record the status
+    # and leave the context usable
+    C.read_status(True)
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    C.flag_wait_probe(flag, 1, 0.05)
+    torch.cuda.synchronize()
+    st = C.read_status(True)
+    assert st[0] == 2 and st[1] == 299
+    x = bf(4, 256)
+    out = torch.empty_like(x)
+    C.rms_norm(out, x, bf(256), 1e-5)
+    torch.cuda.synchronize()
