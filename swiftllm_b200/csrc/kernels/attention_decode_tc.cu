@@ -5,7 +5,7 @@
 // paged_decode dispatches here when it can.
 //
 // Per warp and per 16-token page:
-//   * the page's K and V tiles arrive by 2-D TMA (cp.async.bulk.tensor, no
+//   * the page's K and V tiles arrive by 2-D TMA (cp.async.bulk.tensor,
 //     per-CTA loads) with the 128-byte swizzle, so ldmatrix reads them without
 //     bank conflicts; each warp owns a 2-stage ring and mbarriers;
 //   * S = Q K^T with mma.m16n8k16 (bf16 in, fp32 out): the MMA rows are the
