@@ -17,6 +17,7 @@ from __future__ import annotations
 import asyncio
 import itertools
 import threading
+import time
 import uuid
 from typing import Any, AsyncIterator, Dict, List, Optional, Union
 
@@ -131,6 +132,8 @@ class AsyncLLM:
         self._stop = False
         self._thread: Optional[threading.Thread] = None
         self._error: Optional[BaseException] = None
+        self._stats: Dict[str, Any] = {}
+        self._stats_t = 0.0
 
     @property
     def engine(self) -> LLMEngine:
@@ -170,6 +173,12 @@ class AsyncLLM:
                     continue
                 for out in eng.step():
                     self._deliver(out.request_id, out)
+                now = time.monotonic()
+                if now - self._stats_t > 0.25:
+                    snap = eng.stats()
+                    with self._lock:
+                        self._stats = snap
+                    self._stats_t = now
         except BaseException as ex:  # engine failure ends every stream
             self._error = ex
             with self._lock:
@@ -217,6 +226,15 @@ class AsyncLLM:
                 if rid not in self._aborts:
                     self._aborts.append(rid)  # no-op if it already finished
             self._wake.set()
+
+    def stats(self) -> Dict[str, Any]:
+        """Engine counters (a snapshot the engine thread refreshes every
+        250 ms; read directly when the thread is not running)."""
+        if self._thread is None:
+            self._engine._ensure_initialized()
+            return self._engine.stats()
+        with self._lock:
+            return dict(self._stats)
 
     async def abort(self, request_id: str) -> None:
         with self._lock:
