@@ -35,6 +35,13 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
 void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
                   int64_t red_off, torch::Tensor epochs, double timeout_s);
 void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s);
+int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor offsets,
+                     int64_t avg_rows);
+void moe_route(torch::Tensor logits, int64_t k, bool renorm, torch::Tensor w_out,
+               torch::Tensor id_out);
+void moe_permute(torch::Tensor ids, int64_t e0, int64_t E_local, torch::Tensor offsets,
+                 torch::Tensor perm_token, torch::Tensor inv_slot);
+void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor weights, torch::Tensor inv_slot);
 }  // namespace swift
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -57,4 +64,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &swift::gemm_plan);
   m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
+  m.def("gemm_grouped", &swift::gemm_grouped);
+  m.def("moe_route", &swift::moe_route);
+  m.def("moe_permute", &swift::moe_permute);
+  m.def("moe_combine", &swift::moe_combine);
 }

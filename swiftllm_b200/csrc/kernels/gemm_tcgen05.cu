@@ -143,8 +143,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
                         int64_t ldy, const __nv_bfloat16* __restrict__ bias,
-                        float* __restrict__ ws, int M, int N, int K, int splits, int* status) {
+                        float* __restrict__ ws, int M, int N, int K, int splits, int* status,
+                        const int32_t* __restrict__ goff, int groups) {
   using S = GemmSmem<BN, STAGES>;
+  // Grouped mode (goff != nullptr, MoE experts): group g multiplies the token
+  // rows [goff[g], goff[g+1]) by weight rows [g*M, (g+1)*M); tiles never
+  // straddle groups, rows past a group's end are loaded but not stored.
+  __shared__ int g_off[65];
+  __shared__ int g_tiles[65];
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -160,7 +166,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int n_tiles = (N + BN - 1) / BN;
   const int k_iters = (K + kGemmBK - 1) / kGemmBK;
   const int k_per = (k_iters + splits - 1) / splits;
-  const int total = m_tiles * n_tiles * splits;
+  int total = m_tiles * n_tiles * splits;
+  if (goff) {
+    if (threadIdx.x == 0) {
+      int acc = 0;
+      for (int g = 0; g < groups; ++g) {
+        g_off[g] = goff[g];
+        g_tiles[g] = acc;
+        acc += m_tiles * ((goff[g + 1] - goff[g] + BN - 1) / BN);
+      }
+      g_off[groups] = goff[groups];
+      g_tiles[groups] = acc;
+    }
+    __syncthreads();
+    total = g_tiles[groups];
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -187,11 +207,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   // tile -> (split outermost, then m, n fastest: CTAs running at the same
   // time share the weight tile through L2)
-  auto decode_tile = [&](int t, int& m, int& n, int& s) {
+  // -> split s, feature tile m, first token row x0, token row limit xend,
+  // first weight row w0
+  auto decode_tile = [&](int t, int& m, int& x0, int& xend, int& w0, int& s) {
+    if (goff) {
+      int g = 0;
+      while (g + 1 < groups && g_tiles[g + 1] <= t) ++g;
+      const int r = t - g_tiles[g];
+      const int nt = (g_off[g + 1] - g_off[g] + BN - 1) / BN;
+      m = r / nt;
+      x0 = g_off[g] + (r % nt) * BN;
+      xend = g_off[g + 1];
+      w0 = g * M + m * kGemmBM;
+      s = 0;
+      return;
+    }
     s = t / (m_tiles * n_tiles);
     int r = t % (m_tiles * n_tiles);
     m = r / n_tiles;
-    n = r % n_tiles;
+    x0 = (r % n_tiles) * BN;
+    xend = N;
+    w0 = m * kGemmBM;
   };
 
   if (warp == 0) {
@@ -199,8 +235,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int m, n, s;
-        decode_tile(t, m, n, s);
+        int m, x0, xend, w0, s;
+        decode_tile(t, m, x0, xend, w0, s);
         const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
         for (int kk = k0; kk < k1; ++kk, ++it) {
           const int st = it % STAGES;
@@ -210,8 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
-          tma_load_2d(a, &tm_w, kk * kGemmBK, m * kGemmBM, &full[st]);
-          tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, n * BN, &full[st]);
+          tma_load_2d(a, &tm_w, kk * kGemmBK, w0, &full[st]);
+          tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, x0, &full[st]);
         }
       }
       if (!ok) {  // let the loads already issued land before the CTA exits
@@ -226,8 +262,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tc) {
-        int m, n, s;
-        decode_tile(t, m, n, s);
+        int m, x0, xend, w0, s;
+        decode_tile(t, m, x0, xend, w0, s);
         const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
         const uint32_t buf = tc & 1;
         if (!wait_or_abort(&tempty[buf], ((tc >> 1) & 1) ^ 1, abort_flag, status, 11)) {
@@ -264,8 +300,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
-      int m, n, s;
-      decode_tile(t, m, n, s);
+      int m, x0, xend, w0, s;
+      decode_tile(t, m, x0, xend, w0, s);
       const uint32_t buf = tc & 1;
       bool ok = true;
       for (uint32_t i = 0;; ++i) {
@@ -290,12 +326,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
-          const int t0 = n * BN + c * 32;
+          const int t0 = x0 + c * 32;
           if (f < M) {
             if (splits == 1) {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (t0 + j < N) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+                if (t0 + j < xend) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -306,12 +342,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else {
         float v[16];
         tmem_ld16(tbase, v);
-        const int t0 = n * BN;
+        const int t0 = x0;
         if (f < M) {
           if (splits == 1) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (t0 + j < N) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+              if (t0 + j < xend) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -386,7 +422,8 @@ static int num_sms() {
 
 template <int BN, int STAGES>
 static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloat16* y, int64_t ldy,
-                        const __nv_bfloat16* bias, float* ws, int M, int N, int K, int splits) {
+                        const __nv_bfloat16* bias, float* ws, int M, int N, int K, int splits,
+                        const int32_t* goff = nullptr, int groups = 0) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES>;
   static bool attr[64] = {false};
@@ -397,10 +434,11 @@ static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloa
                                           static_cast<int>(S::BYTES)));
     attr[dev] = true;
   }
-  const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN) * splits;
+  // grouped: tile count is only known on the device; N bounds it
+  const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN + (goff ? groups : 0)) * splits;
   const int grid = std::min(tiles, num_sms());
   kern<<<grid, kGemmThreads, S::BYTES, cur_stream()>>>(tw, tx, y, ldy, bias, ws, M, N, K, splits,
-                                                       status_word_ptr());
+                                                       status_word_ptr(), goff, groups);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -482,6 +520,43 @@ std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
   int bn, s;
   plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), &bn, &s);
   return {bn, s};
+}
+
+}  // namespace swift
+
+namespace swift {
+
+// Grouped GEMM for MoE experts: out [n_max, M] rows of group g (token rows
+// [offsets[g], offsets[g+1]) of x [n_max, K]) = x_rows . w[g]^T with
+// w [groups, M, K]. offsets (int32, groups + 1) live on the device, so the
+// call needs no host synchronisation and can be captured in a CUDA graph.
+int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor offsets,
+                     int64_t avg_rows) {
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(out);
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && x.is_contiguous() && out.is_contiguous());
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.numel() == w.size(0) + 1);
+  const int groups = static_cast<int>(w.size(0));
+  TORCH_CHECK(groups <= 64, "at most 64 groups");
+  const int64_t M = w.size(1), K = w.size(2), T = x.size(0);
+  TORCH_CHECK(x.size(1) == K && K % 8 == 0);
+  if (T == 0) return 0;
+  int bn = 16;
+  while (bn < avg_rows && bn < 256) bn *= 2;
+  CUtensorMap tw = make_tmap(w.data_ptr(), groups * M, K, K, kGemmBM);
+  CUtensorMap tx = make_tmap(x.data_ptr(), T, K, K, bn);
+  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+  const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K);
+  const int32_t* go = offsets.data_ptr<int32_t>();
+  switch (bn) {
+    case 16: launch_gemm<16, 8>(tw, tx, y, M, nullptr, nullptr, Mi, Ni, Ki, 1, go, groups); break;
+    case 32: launch_gemm<32, 8>(tw, tx, y, M, nullptr, nullptr, Mi, Ni, Ki, 1, go, groups); break;
+    case 64: launch_gemm<64, 8>(tw, tx, y, M, nullptr, nullptr, Mi, Ni, Ki, 1, go, groups); break;
+    case 128: launch_gemm<128, 6>(tw, tx, y, M, nullptr, nullptr, Mi, Ni, Ki, 1, go, groups); break;
+    default: launch_gemm<256, 4>(tw, tx, y, M, nullptr, nullptr, Mi, Ni, Ki, 1, go, groups); break;
+  }
+  return 1;
 }
 
 }  // namespace swift

@@ -100,6 +100,12 @@ class DecoderModel:
             self.local_kv_heads = 1
             self.kv_head_start = r * cfg.num_kv_heads // n
         self.local_inter = cfg.intermediate_size // n
+        # MoE: expert parallel when the experts divide over the ranks (each rank
+        # keeps E/n whole experts), else every rank keeps an I/n slice of all
+        self.ep = bool(cfg.num_experts) and n > 1 and cfg.num_experts % n == 0
+        self.e_local = cfg.num_experts // n if self.ep else cfg.num_experts
+        self.e0 = r * self.e_local if self.ep else 0
+        self.moe_inter = cfg.intermediate_size if self.ep else self.local_inter
         if cfg.intermediate_size % n:
             raise ValueError("intermediate_size must be divisible by tensor_parallel_size")
         self.vocab_start, self.vocab_end = 0, cfg.vocab_size
@@ -139,8 +145,8 @@ class DecoderModel:
                 L.ln2_b = None
             if c.num_experts:
                 L.router = self._alloc(c.num_experts, H)
-                L.w13 = self._alloc(c.num_experts, 2 * self.local_inter, H)
-                L.w2 = self._alloc(c.num_experts, H, self.local_inter)
+                L.w13 = self._alloc(self.e_local, 2 * self.moe_inter, H)
+                L.w2 = self._alloc(self.e_local, H, self.moe_inter)
             elif c.hidden_act.startswith("gelu"):
                 L.w1 = self._alloc(self.local_inter, H)
                 L.b1 = self._alloc(self.local_inter) if c.mlp_bias else None
@@ -204,6 +210,8 @@ class DecoderModel:
             i0 = r * self.local_inter
             return ("rows", 2 * I, [(0, i0, self.local_inter),
                                     (self.local_inter, I + i0, self.local_inter)])
+        if leaf in ("w13", "w2") and c.num_experts and self.ep:
+            return ("exp", self.e0)
         if leaf == "w13" and c.num_experts:
             I = c.intermediate_size
             i0 = r * self.local_inter

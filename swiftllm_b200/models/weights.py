@@ -57,13 +57,24 @@ def load_hf_weights(model, get: Callable[[str], Optional[torch.Tensor]]) -> None
         if hasattr(L, "ln2"):
             _copy(L.ln2, need(p + "post_attention_layernorm.weight"), "ln2")
         if c.num_experts:
+            fused = get(p + "mlp.experts.gate_up_proj")  # transformers >= 5 layout
+            if fused is not None:
+                _copy(L.router, need(p + "mlp.gate.weight"), "router")
+                Ifull = c.intermediate_size
+                mi0, mi = (0, Ifull) if model.ep else (I0, In)
+                sl = slice(model.e0, model.e0 + model.e_local)
+                gu = fused[sl]
+                _copy(L.w13, torch.cat([gu[:, mi0:mi0 + mi], gu[:, Ifull + mi0:Ifull + mi0 + mi]], 1), "w13")
+                _copy(L.w2, need(p + "mlp.experts.down_proj")[sl][:, :, mi0:mi0 + mi], "w2")
+                continue
             _copy(L.router, need(p + "block_sparse_moe.gate.weight"), "router")
-            for e in range(c.num_experts):
-                q = p + f"block_sparse_moe.experts.{e}."
-                g = need(q + "w1.weight")[I0:I0 + In]
-                u = need(q + "w3.weight")[I0:I0 + In]
-                _copy(L.w13[e], torch.cat([g, u], 0), q + "w13")
-                _copy(L.w2[e], need(q + "w2.weight")[:, I0:I0 + In], q + "w2")
+            mi0, mi = (0, c.intermediate_size) if model.ep else (I0, In)
+            for le in range(model.e_local):
+                q = p + f"block_sparse_moe.experts.{model.e0 + le}."
+                g = need(q + "w1.weight")[mi0:mi0 + mi]
+                u = need(q + "w3.weight")[mi0:mi0 + mi]
+                _copy(L.w13[le], torch.cat([g, u], 0), q + "w13")
+                _copy(L.w2[le], need(q + "w2.weight")[:, mi0:mi0 + mi], q + "w2")
         elif phi or c.hidden_act.startswith("gelu"):
             _copy(L.w1, need(p + "mlp.fc1.weight")[I0:I0 + In], "fc1")
             if L.b1 is not None:

@@ -88,6 +88,11 @@ def fill_normal_sharded(t: torch.Tensor, spec, seed: int, tid: int, std: float) 
         for lo, flo, n in segs:
             _fill_view(t[..., lo:lo + n, :], key, std, full_rows, cols, flo, 0)
         return
+    if kind == "exp":  # expert-parallel shard: local experts start at global e0
+        e0 = spec[1]
+        R, C = t.shape[-2], t.shape[-1]
+        _fill_view(t, key, std, R, C, e0 * R, 0)
+        return
     if kind in ("cols", "cols3"):
         full_cols, col0 = spec[1], spec[2]
         _fill_view(t, key, std, t.shape[-2], full_cols, 0, col0)

@@ -257,3 +257,40 @@ def test_peer_wait_times_out_cleanly(C):
     out = torch.empty_like(x)
     C.rms_norm(out, x, bf(256), 1e-5)
     torch.cuda.synchronize()
+
+
+def test_moe_route_permute_grouped_gemm_combine(C):
+    from swiftllm_b200.ops import reference as R
+    T, E, k, H, I = 37, 8, 2, 256, 192
+    logits = torch.randn(T, E, device="cuda")
+    w = torch.empty(T, k, device="cuda")
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    C.moe_route(logits, k, True, w, ids)
+    rw, rid = R.moe_topk_softmax(logits.cpu(), k)
+    assert torch.equal(ids.cpu(), rid) and torch.allclose(w.cpu(), rw, atol=1e-5)
+    for e0, El in ((0, 8), (4, 4)):
+        off = torch.empty(El + 1, dtype=torch.int32, device="cuda")
+        perm = torch.empty(T * k, dtype=torch.int32, device="cuda")
+        inv = torch.empty(T * k, dtype=torch.int32, device="cuda")
+        C.moe_permute(ids, e0, El, off, perm, inv)
+        x = bf(T, H)
+        w13 = bf(El, 2 * I, H, scale=0.05)
+        w2 = bf(El, H, I, scale=0.05)
+        xg = x.index_select(0, perm)
+        h = torch.empty(T * k, 2 * I, dtype=torch.bfloat16, device="cuda")
+        C.gemm_grouped(h, xg, w13, off, T * k // E)
+        a = torch.empty(T * k, I, dtype=torch.bfloat16, device="cuda")
+        C.silu_and_mul(a, h)
+        y = torch.empty(T * k, H, dtype=torch.bfloat16, device="cuda")
+        C.gemm_grouped(y, a, w2, off, T * k // E)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+        C.moe_combine(out, y, w, inv)
+        ref = torch.zeros(T, H)
+        for le in range(El):
+            rows, slot = (ids.cpu() == e0 + le).nonzero(as_tuple=True)
+            if rows.numel() == 0:
+                continue
+            hh = R.silu_and_mul(x.float().cpu()[rows] @ w13[le].float().cpu().t())
+            ref.index_add_(0, rows, (hh @ w2[le].float().cpu().t()) * w.cpu()[rows, slot].unsqueeze(1))
+        torch.testing.assert_close(out.float().cpu(), ref, rtol=3e-2, atol=3e-2)
+    _status_ok(C)

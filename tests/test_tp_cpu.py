@@ -17,7 +17,7 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen2"])
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen2", "tiny-mixtral"])
 def test_tp2_gloo_matches_tp1(name):
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr", "127.0.0.1", "--master-port", str(_port()),
