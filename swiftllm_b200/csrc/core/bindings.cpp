@@ -258,6 +258,30 @@ PYBIND11_MODULE(_core, m) {
              return s.update(b, toks.data(), lp, now);
            },
            py::arg("batch"), py::arg("tokens"), py::arg("logprobs") = py::none(), py::arg("now") = 0.0)
+      .def("update_multi",
+           [](Scheduler& s, const Batch& b, py::array_t<int32_t, py::array::c_style | py::array::forcecast> toks,
+              py::array_t<int32_t, py::array::c_style | py::array::forcecast> counts,
+              py::object logprobs, double now) {
+             if (static_cast<size_t>(counts.size()) != b.sample_logit_idx.size())
+               throw std::invalid_argument("one count per sample row expected");
+             int64_t total = 0;
+             for (ssize_t i = 0; i < counts.size(); ++i) {
+               if (counts.data()[i] < 0) throw std::invalid_argument("negative count");
+               total += counts.data()[i];
+             }
+             if (total != toks.size()) throw std::invalid_argument("tokens do not match counts");
+             const float* lp = nullptr;
+             py::array_t<float, py::array::c_style | py::array::forcecast> lpa;
+             if (!logprobs.is_none()) {
+               lpa = logprobs.cast<py::array_t<float, py::array::c_style | py::array::forcecast>>();
+               if (lpa.size() != total) throw std::invalid_argument("one logprob per token expected");
+               lp = lpa.data();
+             }
+             return s.update_multi(b, toks.data(), counts.data(), lp, now);
+           },
+           py::arg("batch"), py::arg("tokens"), py::arg("counts"), py::arg("logprobs") = py::none(),
+           py::arg("now") = 0.0)
+      .def("decode_ready_seqs", [](const Scheduler& s) { return to_np(s.decode_ready_seqs()); })
       .def("append_tokens", &Scheduler::append_tokens)
       .def("rollback", &Scheduler::rollback)
       .def_property_readonly("num_waiting", &Scheduler::num_waiting)
@@ -294,6 +318,9 @@ PYBIND11_MODULE(_core, m) {
              d["status"] = status_name(q->status);
              d["cum_logprob"] = q->cum_logprob;
              d["num_output"] = q->num_output();
+             d["num_draft"] = q->num_draft;
+             d["group"] = q->group;
+             d["num_tokens"] = static_cast<int64_t>(q->tokens.size());
              return d;
            })
       .def("seq_tokens",

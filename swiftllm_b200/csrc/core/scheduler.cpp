@@ -195,8 +195,8 @@ std::unique_ptr<Batch> Scheduler::schedule(double now) {
       for (auto& w : want) {
         const Sequence& s = seqs_.at(w.first);
         int64_t end = s.num_computed + w.second;
-        // reserve speculative slots for pure decode steps
-        if (w.second == 1 && extra > 0) end += extra;
+        // reserve speculative slots whenever the step reaches the last token
+        if (extra > 0 && end == static_cast<int64_t>(s.tokens.size())) end += extra;
         need += bm_->blocks_to_grow(w.first, s.num_computed, end);
       }
       if (bm_->can_allocate(need, false)) break;
@@ -214,7 +214,7 @@ std::unique_ptr<Batch> Scheduler::schedule(double now) {
     for (auto& w : want) {
       Sequence& s = seqs_.at(w.first);
       int64_t end = s.num_computed + w.second;
-      if (w.second == 1 && extra > 0) end += extra;
+      if (extra > 0 && end == static_cast<int64_t>(s.tokens.size())) end += extra;
       bm_->ensure_slots(w.first, s.num_computed, end, &out->copies);
       items.push_back({w.first, w.second, gid});
     }
@@ -390,7 +390,7 @@ std::unique_ptr<Batch> Scheduler::schedule(double now) {
     b.seq_ids.push_back(it.seq);
     b.max_q_len = std::max<int>(b.max_q_len, static_cast<int>(it.n));
     b.max_seq_len = std::max<int>(b.max_seq_len, static_cast<int>(end));
-    if (it.n > 1 || s.num_output() == 0) b.num_prefill_tokens += it.n;
+    if ((it.n > 1 && s.num_draft == 0) || s.num_output() == 0) b.num_prefill_tokens += it.n;
     else stats_.decode_tokens += it.n;
     bool samples = end == static_cast<int64_t>(s.tokens.size());
     s.num_computed = end;
@@ -441,6 +441,12 @@ void Scheduler::finish_group_if_done(int64_t gid, double now, StepResult* res) {
 
 StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float* logprobs,
                              double now) {
+  std::vector<int32_t> ones(b.sample_logit_idx.size(), 1);
+  return update_multi(b, tokens, ones.data(), logprobs, now);
+}
+
+StepResult Scheduler::update_multi(const Batch& b, const int32_t* tokens, const int32_t* counts,
+                                   const float* logprobs, double now) {
   StepResult res;
   std::vector<int64_t> touched;
   // register newly full blocks for prefix caching before any sequence of this
@@ -455,6 +461,8 @@ StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float*
     }
   }
   const size_t rows = b.sample_logit_idx.size();
+  std::vector<int64_t> first(rows + 1, 0);
+  for (size_t r = 0; r < rows; ++r) first[r + 1] = first[r] + counts[r];
   // children (n > 1) fork from the parent's prompt before the parent appends
   std::vector<size_t> order;
   order.reserve(rows);
@@ -490,31 +498,38 @@ StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float*
     if (sit == seqs_.end()) continue;
     Sequence& s = sit->second;
     if (s.status != SeqStatus::RUNNING) continue;  // aborted meanwhile
-    int32_t tok = tokens[r];
-    s.tokens.push_back(tok);
-    if (logprobs) s.cum_logprob += logprobs[r];
-    if (g.first_token < 0) g.first_token = now;
-    res.group.push_back(gid);
-    res.seq.push_back(sid);
-    res.token.push_back(tok);
-    res.row.push_back(static_cast<int32_t>(r));
     const GroupParams& p = g.params;
-    int64_t nout = s.num_output();
-    SeqStatus fin = SeqStatus::RUNNING;
-    if (nout >= p.min_tokens) {
-      if (!p.ignore_eos && p.eos_token_id >= 0 && tok == p.eos_token_id)
-        fin = SeqStatus::FINISHED_STOPPED;
-      else if (std::find(p.stop_token_ids.begin(), p.stop_token_ids.end(), tok) !=
-               p.stop_token_ids.end())
-        fin = SeqStatus::FINISHED_STOPPED;
+    for (int64_t q = first[r]; q < first[r + 1]; ++q) {
+      int32_t tok = tokens[q];
+      s.tokens.push_back(tok);
+      if (logprobs) s.cum_logprob += logprobs[q];
+      if (g.first_token < 0) g.first_token = now;
+      res.group.push_back(gid);
+      res.seq.push_back(sid);
+      res.token.push_back(tok);
+      res.row.push_back(static_cast<int32_t>(r));
+      int64_t nout = s.num_output();
+      SeqStatus fin = SeqStatus::RUNNING;
+      if (nout >= p.min_tokens) {
+        if (!p.ignore_eos && p.eos_token_id >= 0 && tok == p.eos_token_id)
+          fin = SeqStatus::FINISHED_STOPPED;
+        else if (std::find(p.stop_token_ids.begin(), p.stop_token_ids.end(), tok) !=
+                 p.stop_token_ids.end())
+          fin = SeqStatus::FINISHED_STOPPED;
+      }
+      if (fin == SeqStatus::RUNNING &&
+          (nout >= p.max_tokens || static_cast<int64_t>(s.tokens.size()) >= cfg_.max_model_len))
+        fin = SeqStatus::FINISHED_LENGTH;
+      if (fin != SeqStatus::RUNNING) {
+        free_seq(s);
+        s.status = fin;
+        break;
+      }
     }
-    if (fin == SeqStatus::RUNNING &&
-        (nout >= p.max_tokens || static_cast<int64_t>(s.tokens.size()) >= cfg_.max_model_len))
-      fin = SeqStatus::FINISHED_LENGTH;
-    if (fin != SeqStatus::RUNNING) {
-      free_seq(s);
-      s.status = fin;
-    }
+    // tokens verified by this step already have their KV; only the newest
+    // one still needs computing
+    if (s.status == SeqStatus::RUNNING)
+      s.num_computed = std::max<int64_t>(s.num_computed, static_cast<int64_t>(s.tokens.size()) - 1);
     touched.push_back(gid);
   }
   std::sort(touched.begin(), touched.end());
@@ -525,7 +540,9 @@ StepResult Scheduler::update(const Batch& b, const int32_t* tokens, const float*
 
 void Scheduler::append_tokens(int64_t sid, const std::vector<int32_t>& toks) {
   Sequence& s = seqs_.at(sid);
+  if (s.status != SeqStatus::RUNNING) throw std::invalid_argument("append to a sequence that is not running");
   s.tokens.insert(s.tokens.end(), toks.begin(), toks.end());
+  s.num_draft += static_cast<int64_t>(toks.size());
 }
 
 void Scheduler::rollback(int64_t sid, int64_t n) {
@@ -533,8 +550,23 @@ void Scheduler::rollback(int64_t sid, int64_t n) {
   if (n <= 0) return;
   if (n > s.num_output()) throw std::invalid_argument("rollback past the prompt");
   s.tokens.resize(s.tokens.size() - n);
-  if (s.num_computed > static_cast<int64_t>(s.tokens.size()))
-    s.num_computed = static_cast<int64_t>(s.tokens.size());
+  s.num_draft = std::max<int64_t>(0, s.num_draft - n);
+  const int64_t last = static_cast<int64_t>(s.tokens.size()) - 1;
+  if (s.num_computed > last) s.num_computed = last;
+}
+
+std::vector<int64_t> Scheduler::decode_ready_seqs() const {
+  std::vector<int64_t> out;
+  for (int64_t gid : running_) {
+    const Group& g = groups_.at(gid);
+    for (int64_t sid : g.seqs) {
+      const Sequence& s = seqs_.at(sid);
+      if (s.status == SeqStatus::RUNNING && s.num_output() > 0 &&
+          s.num_computed + 1 == static_cast<int64_t>(s.tokens.size()))
+        out.push_back(sid);
+    }
+  }
+  return out;
 }
 
 const Group* Scheduler::group(int64_t gid) const {

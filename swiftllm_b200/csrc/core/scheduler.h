@@ -80,6 +80,7 @@ struct Sequence {
   int64_t num_computed = 0;
   SeqStatus status = SeqStatus::WAITING;
   double cum_logprob = 0.0;
+  int64_t num_draft = 0;  // trailing speculative tokens awaiting verification
   int64_t num_output() const { return static_cast<int64_t>(tokens.size()) - num_prompt; }
 };
 
@@ -158,10 +159,20 @@ class Scheduler {
   StepResult update(const Batch& batch, const int32_t* tokens, const float* logprobs,
                     double now);
 
-  // spec decode: set the draft tokens of a running seq (appended provisionally)
-  // and roll back rejected ones.
+  // Speculative decoding. append_tokens adds draft tokens to a running
+  // sequence, so the next schedule() computes them together with the last
+  // real token (query length 1 + k). rollback(seq, n) removes n trailing
+  // tokens (the drafts) and marks the last remaining token uncomputed, so a
+  // sequence whose drafts were not verified is recomputed from there.
+  // update_multi then appends the verified tokens of each sample row
+  // (counts[r] tokens starting at offsets[r]) with the stop rules applied per
+  // token; every appended token but the last keeps the KV written for it.
   void append_tokens(int64_t seq, const std::vector<int32_t>& toks);
   void rollback(int64_t seq, int64_t num_tokens);
+  StepResult update_multi(const Batch& batch, const int32_t* tokens, const int32_t* counts,
+                          const float* logprobs, double now);
+  // running sequences whose next step is a plain decode (one token to compute)
+  std::vector<int64_t> decode_ready_seqs() const;
 
   int num_waiting() const { return static_cast<int>(waiting_.size()); }
   int num_running() const { return static_cast<int>(running_.size()); }

@@ -106,6 +106,9 @@ class LLMEngine:
         self.eos_token_id = getattr(self.tokenizer, "eos_token_id", None)
         if self.eos_token_id is None:
             self.eos_token_id = mcfg.eos_token_id
+        if c.speculative_model:
+            from .speculative import reserve_draft_memory
+            reserve_draft_memory(c)
         self.executor = make_executor(mcfg, c)
         num_gpu, num_cpu = self.executor.num_gpu_blocks, self.executor.num_cpu_blocks
         self.block_manager = _core.BlockManager(c.block_size, num_gpu, num_cpu, c.watermark,
@@ -119,6 +122,8 @@ class LLMEngine:
                      SchedulerPolicy.PRIORITY: _core.Policy.PRIORITY}[c.scheduler_policy]
         sc.preemption = (_core.Preempt.SWAP if c.preemption_mode == PreemptionMode.SWAP and num_cpu > 0
                          else _core.Preempt.RECOMPUTE)
+        if c.speculative_model:
+            sc.num_speculative_tokens = int(c.num_speculative_tokens)
         self.scheduler = _core.Scheduler(sc, self.block_manager)
         self.sampler = BatchSampler(mcfg.vocab_size, c.seed, self.executor.device)
         if c.speculative_model:
@@ -205,12 +210,7 @@ class LLMEngine:
             return outs + self.spec.step()
         with nvtx.range("schedule"):
             b = self.scheduler.schedule(time.monotonic())
-        for g in b.preempted_groups:
-            if g < 0:  # rejected: prompt can never fit the KV pool
-                r = self._by_gid.get(-g)
-                if r is not None:
-                    log.warning("request %s rejected: prompt exceeds KV cache capacity", r.request_id)
-                    outs.append(self._final_output(r))
+        outs += self._rejected(b)
         if b.num_seqs == 0 and b.swap_in.size == 0 and b.swap_out.size == 0:
             return outs
         from ..runtime.model_runner import step_input_from_batch
@@ -225,19 +225,33 @@ class LLMEngine:
             return outs
         with nvtx.range("sample"):
             toks, lps = self.sampler(logits, b, self._history)
-        want_lp = None
-        if any(self._by_gid[g].params.logprobs for g in set(np.asarray(b.sample_group).tolist())
-               if g in self._by_gid):
-            want_lp = self._top_logprobs(logits, b, toks)
+        want_lp = self._top_logprobs(logits, b, toks) if self._wants_logprobs(b) else None
         res = self.scheduler.update(b, toks, lps, time.monotonic())
         self._gen_tokens += len(res.token)
-        self.last_step_tokens = len(res.token)
+        self._account(si, b, len(res.token))
+        return outs + self._process(res, want_lp)
+
+    def _rejected(self, b) -> List[RequestOutput]:
+        outs = []
+        for g in b.preempted_groups:
+            if g < 0:  # rejected: prompt can never fit the KV pool
+                r = self._by_gid.get(-g)
+                if r is not None:
+                    log.warning("request %s rejected: prompt exceeds KV cache capacity", r.request_id)
+                    outs.append(self._final_output(r))
+        return outs
+
+    def _wants_logprobs(self, b) -> bool:
+        return any(self._by_gid[g].params.logprobs for g in set(np.asarray(b.sample_group).tolist())
+                   if g in self._by_gid)
+
+    def _account(self, si, b, ntok: int) -> None:
+        self.last_step_tokens = ntok
         self.io_bytes[0] += si.ints.nbytes + si.logits_idx.nbytes + 28 * int(b.num_sample_rows)
         self.io_bytes[1] += 8 * int(b.num_sample_rows)
         self.num_steps += 1
         if self.step_hook is not None:
             self.step_hook(self)
-        return outs + self._process(res, want_lp)
 
     def _top_logprobs(self, logits, b, toks):
         import torch

@@ -162,7 +162,10 @@ class ModelRunner:
         used_by_others = total - free - torch.cuda.memory_reserved(self.device)
         budget = total * self.ecfg.gpu_memory_utilization - (peak - kv_now) - max(used_by_others, 0)
         budget -= 2 << 30  # graphs, sampler scratch, NCCL / comm buffers
-        n = int(budget // self.block_bytes())
+        # a speculative draft model keeps its weights and one KV block per
+        # target block on the same GPU
+        budget -= getattr(self.ecfg, "draft_reserve_bytes", 0)
+        n = int(budget // (self.block_bytes() + getattr(self.ecfg, "draft_block_bytes", 0)))
         if n <= 0:
             raise RuntimeError("no GPU memory left for the KV cache; lower max_num_batched_tokens "
                                "or raise gpu_memory_utilization")
