@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import os
 import pickle
+import threading
 import time
 import uuid
 from typing import Optional
@@ -31,6 +32,10 @@ log = get_logger(__name__)
 
 _SHUTDOWN = b"__shutdown__"
 STEP_TIMEOUT = float(os.environ.get("SWIFTLLM_STEP_TIMEOUT", "600"))
+# a worker whose heartbeat is older than this is reported dead; workers
+# likewise give up on an engine whose heartbeat stopped
+PEER_TIMEOUT = float(os.environ.get("SWIFTLLM_PEER_TIMEOUT", "60"))
+HEARTBEAT_PERIOD = 0.5
 
 
 def _device_for(cfg, local_rank: int) -> torch.device:
@@ -79,7 +84,11 @@ def worker_loop(model_cfg, cfg, rank: int, world: int, local_rank: int, channel_
     if ch is None:
         raise RuntimeError("worker could not attach to the control channel")
     while True:
-        msg = ch.receive(timeout=-1.0, peer_timeout=STEP_TIMEOUT)
+        try:
+            msg = ch.receive(timeout=-1.0, peer_timeout=PEER_TIMEOUT)
+        except _core.PeerDiedError as e:
+            log.error("rank %d: %s; exiting", rank, e)
+            raise SystemExit(3)
         if msg == _SHUTDOWN:
             break
         obj = pickle.loads(msg)
@@ -189,6 +198,10 @@ class LocalExecutor:
                 os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port)})
                 init_distributed(0, world, self._backend())
             self.channel = _core.ShmChannel(cname, True, world - 1, -1, 8, 16 << 20)
+            self._beat_stop = threading.Event()
+            self._beat = threading.Thread(target=self._beat_loop, name="swiftllm-heartbeat",
+                                          daemon=True)
+            self._beat.start()
         self.runner = _build_runner(model_cfg, cfg, 0, world, local_rank if env_world == world else 0)
         self.device = self.runner.device
         self.num_gpu_blocks = self.runner.num_gpu_blocks
@@ -209,15 +222,31 @@ class LocalExecutor:
             self.channel.publish(pickle.dumps(si, protocol=pickle.HIGHEST_PROTOCOL), STEP_TIMEOUT)
         return self.runner.execute(si)
 
+    def _beat_loop(self) -> None:
+        # the engine's heartbeat: workers waiting for a step see it advance
+        # even when no request arrives for a long time
+        ch = self.channel
+        while not self._beat_stop.wait(HEARTBEAT_PERIOD):
+            if ch is None or ch.closed:
+                break
+            ch.beat()
+
     def _check_workers(self) -> None:
+        from .failures import WorkerDiedError
         for p in self.procs:
             if not p.is_alive():
-                from .failures import WorkerDiedError
                 raise WorkerDiedError(f"tensor-parallel worker pid {p.pid} exited "
                                       f"(code {p.exitcode})")
+        for r in range(1, self.world):
+            age = self.channel.heartbeat_age(r)
+            # age > 1e6 s: the worker has not attached yet (still loading)
+            if PEER_TIMEOUT < age < 1e6:
+                raise WorkerDiedError(f"tensor-parallel rank {r} heartbeat lost "
+                                      f"({age:.1f} s old)")
 
     def shutdown(self) -> None:
         if self.channel is not None:
+            self._beat_stop.set()
             try:
                 self.channel.publish(_SHUTDOWN, 5.0)
             except Exception:
