@@ -32,6 +32,9 @@ void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch
             torch::Tensor iparams, torch::Tensor keys, bool any_random);
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
+torch::Tensor gemm_sk_stamps();
+int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
+                    c10::optional<torch::Tensor> bias);
 void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
                   int64_t red_off, torch::Tensor epochs, double timeout_s);
 void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s);
@@ -62,6 +65,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &swift::sample);
   m.def("gemm", &swift::gemm);
   m.def("gemm_plan", &swift::gemm_plan);
+  m.def("gemm_sk_stamps", &swift::gemm_sk_stamps);
+  m.def("gemm_packed", &swift::gemm_packed);
   m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
   m.def("gemm_grouped", &swift::gemm_grouped);

@@ -29,6 +29,9 @@
 // freed and the CTA returns.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace swift {
@@ -369,6 +372,395 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ stream-K
+// Decode-shaped GEMMs (at most 256 tokens): one token tile covers every
+// token, so the weight is read exactly once; a CTA owns MT x 128 features at
+// a time, so the token tile is re-read from L2 only M / (128 MT) times. The
+// (tile, k-iteration) space is cut into one contiguous range per CTA (all
+// SMs busy, no wave tail). A tile whose K range spans several CTAs is
+// finished by whichever CTA arrives last: every CTA writes its fp32 partial
+// to its own workspace slot, fences, bumps the tile's counter; the one that
+// sees the count complete adds the other partials and stores bf16 (and resets
+// the counter for the next launch). No CTA ever waits for another.
+constexpr int pow2_cols(int c) { return c <= 32 ? 32 : c <= 64 ? 64 : c <= 128 ? 128 : c <= 256 ? 256 : 512; }
+
+template <int BN, int MT, int STAGES>
+struct SkSmem {
+  static constexpr int UM = kGemmBM * MT;
+  static constexpr int A_BYTES = UM * kGemmBK * 2;
+  static constexpr int B_BYTES = BN * kGemmBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int ACC_COLS = MT * BN;
+  static constexpr int NBUF = 2 * ACC_COLS <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = pow2_cols(NBUF * ACC_COLS);
+  static constexpr size_t BYTES = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int BN, int MT, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_streamk_kernel(const __grid_constant__ CUtensorMap tm_w,
+                        const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
+                        int64_t ldy, const __nv_bfloat16* __restrict__ bias,
+                        float* __restrict__ ws, int* __restrict__ counters, int M, int N, int K,
+                        int per, int* status, int probe, int vec_out,
+                        unsigned long long* __restrict__ stamps, int packed_kt, int rot_mul) {
+  using S = SkSmem<BN, MT, STAGES>;
+  constexpr int UM = S::UM, NBUF = S::NBUF;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int sh_last;
+  __shared__ int sh_ok[2][4];
+  __shared__ __align__(8) uint64_t fixbar;  // partner partials fetched into the idle ring
+  __shared__ __align__(16) __nv_bfloat16 epi_stage[4 * 32 * 40];
+  uint8_t* tiles =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + size_t(STAGES) * S::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int m_units = (M + UM - 1) / UM;
+  const int k_iters = (K + kGemmBK - 1) / kGemmBK;
+  const int total = m_units * n_tiles * k_iters;
+  const int cta = blockIdx.x;
+  const int it_begin = min(total, cta * per), it_end = min(total, it_begin + per);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(&fixbar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(S::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // measurement probe bit 4: epilogue thread 64 records %globaltimer at phase
+  // boundaries (kernel start, per segment: accumulator ready, partial
+  // stored, done) into stamps[cta][16]
+  auto stamp = [&](int k) {
+    if ((probe & 4) && threadIdx.x == 64 && k < 16) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      stamps[cta * 16 + k] = t;
+    }
+  };
+  stamp(0);
+
+  // Segments of this CTA's range, natural order j = 0..nseg-1 (tile
+  // first_tile + j). Processing order: a partial LAST segment goes first
+  // (it is the beginning of a tile whose end the next CTA computes as its
+  // first processed segment), then the rest in order. So both halves of a
+  // split tile are computed early, and the CTA that finishes the tile finds
+  // the other partials ready and never stores its own.
+  const int first_tile = it_begin / k_iters;
+  const int nseg = it_end > it_begin ? (it_end - 1) / k_iters - first_tile + 1 : 0;
+  const bool tail_first = nseg >= 2 && ((it_end - 1) % k_iters + 1) < k_iters;
+  auto seg_of = [&](int p, int& j, int& t, int& k0, int& k1) {
+    j = tail_first ? (p == 0 ? nseg - 1 : p - 1) : p;
+    t = first_tile + j;
+    k0 = j == 0 ? it_begin % k_iters : 0;
+    k1 = j == nseg - 1 ? (it_end - 1) % k_iters + 1 : k_iters;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int p = 0; p < nseg && ok; ++p) {
+        int j, t, k0, k1;
+        seg_of(p, j, t, k0, k1);
+        const int w0 = (t / n_tiles) * UM, x0 = (t % n_tiles) * BN;
+        const int len = k1 - k0, rot = rot_mul ? (cta * rot_mul) % len : 0;
+        for (int kq = k0; kq < k1; ++kq, ++it) {
+          // optional rotation of the K order per CTA (measurement knob)
+          const int kk = rot ? k0 + (kq - k0 + rot) % len : kq;
+          const int st = it % STAGES;
+          if (!wait_or_abort(&empty[st], ((it / STAGES) & 1) ^ 1, abort_flag, status, 20)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
+          if ((probe & 3) == 2) {  // measurement probe: no loads (tensor-pipe time alone)
+            mbar_arrive(&full[st]);
+            continue;
+          }
+          // probe bits 16 / 32 (measurement): skip the weight / token loads
+          mbar_arrive_expect_tx(&full[st], (probe & 16 ? 0 : S::A_BYTES) + (probe & 32 ? 0 : S::B_BYTES));
+          if (probe & 16) {
+          } else if (packed_kt) {  // tile-packed weights: one contiguous 16 KB box per 128 rows
+#pragma unroll
+            for (int mi = 0; mi < MT; ++mi)
+              tma_load_2d(a + mi * kGemmBM * kGemmBK * 2, &tm_w, 0,
+                          ((w0 / kGemmBM + mi) * packed_kt + kk) * kGemmBM, &full[st]);
+          } else {
+            tma_load_2d(a, &tm_w, kk * kGemmBK, w0, &full[st]);
+          }
+          if (!(probe & 32)) tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, x0, &full[st]);
+        }
+      }
+      if (!ok) {
+        for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+          for (uint32_t p = 0; p < (1u << 20); ++p)
+            if (mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = instr_desc_bf16<BN>();
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int p = 0; p < nseg && ok; ++p, ++tc) {
+        int j, t, k0, k1;
+        seg_of(p, j, t, k0, k1);
+        const uint32_t buf = tc % NBUF;
+        if (!wait_or_abort(&tempty[buf], ((tc / NBUF) & 1) ^ 1, abort_flag, status, 21)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * S::ACC_COLS;
+        for (int kk = k0; kk < k1; ++kk, ++it) {
+          const int st = it % STAGES;
+          if (!wait_or_abort(&full[st], (it / STAGES) & 1, abort_flag, status, 22)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
+          const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
+#pragma unroll
+          for (int q = 0; q < kGemmBK / 16; ++q) {
+            if ((probe & 3) == 1) break;  // measurement probe: no MMAs (load time alone)
+#pragma unroll
+            for (int i = 0; i < MT; ++i) {
+              const uint64_t ad = smem_desc_sw128(a + i * kGemmBM * kGemmBK * 2);
+              umma_bf16(d_tmem + i * BN, ad + 2 * q, bd + 2 * q, idesc,
+                        (kk > k0 || q > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+      }
+      if (!ok) {
+        for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+          for (uint32_t p = 0; p < (1u << 20); ++p)
+            if (mbar_try_wait(&empty[j % STAGES], (j / STAGES) & 1)) break;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int slot_floats = UM * BN;
+    uint32_t tc = 0, fix_uses = 0;
+    for (int p = 0; p < nseg; ++p, ++tc) {
+      int j, t, k0, k1;
+      seg_of(p, j, t, k0, k1);
+      const int m0 = (t / n_tiles) * UM, x0 = (t % n_tiles) * BN;
+      const uint32_t buf = tc % NBUF;
+      bool ok = true;
+      for (uint32_t i = 0;; ++i) {
+        bool r = mbar_try_wait(&tfull[buf], (tc / NBUF) & 1);
+        if (__all_sync(0xffffffffu, r)) break;
+        if (i > kWaitLimit || ((i & 255) == 255 && *abort_flag)) {
+          if (lane == 0 && i > kWaitLimit) {
+            set_status(status, kErrWaitTimeout, 23);
+            *abort_flag = 1;
+          }
+          ok = false;
+          break;
+        }
+      }
+      // the four epilogue warps agree before any named barrier, so a warp
+      // that gave up never leaves the others waiting at bar.sync
+      if (lane == 0) sh_ok[tc & 1][q] = ok;
+      epi_bar();
+      ok = sh_ok[tc & 1][0] && sh_ok[tc & 1][1] && sh_ok[tc & 1][2] && sh_ok[tc & 1][3];
+      if (!ok) break;
+      tc_fence_after();
+      stamp(1 + 3 * p);
+      // probe bit 64 (measurement, wrong results): every segment treated as
+      // a whole tile (no partials, no fix-up)
+      const bool whole = (k0 == 0 && k1 == k_iters) || (probe & 64);
+      const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * S::ACC_COLS;
+      const int fl = q * 32 + lane;  // feature within a 128-row sub-tile
+      bool last = whole;
+      int cf = 0, cl = -1;
+      if (!whole) {
+        cf = (t * k_iters) / per;
+        cl = ((t + 1) * k_iters - 1) / per;
+        // every other CTA of this tile already done? then this one finishes
+        // it without storing its own partial
+        if (threadIdx.x == 64) {
+          int done = *reinterpret_cast<volatile int*>(&counters[t]);
+          int lst = done == cl - cf;
+          if (lst) {
+            __threadfence();  // acquire the other partials
+            counters[t] = 0;
+          }
+          sh_last = lst;
+        }
+        epi_bar();
+        last = sh_last != 0;
+        epi_bar();
+        if (!last) {
+          // partial slot layout: [token column (BN)][feature (UM)] fp32: a
+          // warp moves 32 consecutive features of one column per instruction
+          float* wp = ws + size_t(j == 0 ? 2 * cta : 2 * cta + 1) * slot_floats;
+#pragma unroll 1
+          for (int i = 0; i < MT; ++i)
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              float v[32];
+              tmem_ld32(tq + i * BN + c * 32, v);
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                __stcg(wp + size_t(c * 32 + jj) * UM + i * kGemmBM + fl, v[jj]);
+            }
+          // release: the partial stores happen-before the counter bump
+          epi_bar();
+          if (threadIdx.x == 64) {
+            __threadfence();
+            const int old = atomicAdd(&counters[t], 1);
+            const int lst = old == cl - cf;
+            if (lst) {
+              __threadfence();
+              counters[t] = 0;
+            }
+            sh_last = lst;
+          }
+          epi_bar();
+          last = sh_last != 0;
+        }
+        stamp(2 + 3 * p);
+      }
+      // The CTA's last processed segment: producer and MMAs are done, so the
+      // other CTAs' partials are fetched with bulk copies into the idle
+      // shared-memory ring (one latency instead of one per chunk).
+      const int others = whole ? 0 : cl - cf;
+      const bool staged = last && others > 0 && p == nseg - 1 && !(probe & 8) &&
+                          size_t(others) * slot_floats * 4 <= size_t(STAGES) * S::STAGE_BYTES;
+      if (staged) {
+        if (threadIdx.x == 64) {
+          asm volatile("fence.proxy.async;" ::: "memory");
+          constexpr uint32_t kPiece = 32768;
+          const uint32_t slot_bytes = uint32_t(slot_floats) * 4;
+          mbar_arrive_expect_tx(&fixbar, uint32_t(others) * slot_bytes);
+          int idx = 0;
+          for (int o = cf; o <= cl; ++o) {
+            if (o == cta) continue;
+            const int slot = ((o * per) / k_iters == t) ? 2 * o : 2 * o + 1;
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(ws + size_t(slot) * slot_floats);
+            for (uint32_t off = 0; off < slot_bytes; off += kPiece)
+              bulk_g2s(tiles + size_t(idx) * slot_bytes + off, src + off,
+                       min(kPiece, slot_bytes - off), &fixbar);
+            ++idx;
+          }
+        }
+        if (!mbar_wait_warp(&fixbar, fix_uses & 1, status, 24)) *abort_flag = 1;
+        ++fix_uses;
+      }
+      if (last) {
+        __nv_bfloat16* stage = epi_stage + q * 32 * 40;  // [32 tokens][40] bf16, padded rows
+#pragma unroll 1
+        for (int i = 0; i < MT; ++i) {
+          const int f = m0 + i * kGemmBM + fl;
+          const float b = (bias != nullptr && f < M) ? __bfloat162float(bias[f]) : 0.f;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float own[32], v[32];
+            tmem_ld32(tq + i * BN + c * 32, own);
+            // fixed summation order over the tile's CTAs (bitwise identical
+            // results whichever CTA finishes the tile)
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) v[jj] = (cf == cta || whole) ? own[jj] : 0.f;
+            int idx = 0;
+            for (int o = cf; o <= cl; ++o) {
+              if (o == cta) {
+                if (o != cf) {
+#pragma unroll
+                  for (int jj = 0; jj < 32; ++jj) v[jj] += own[jj];
+                }
+                continue;
+              }
+              const size_t off = size_t(c * 32) * UM + i * kGemmBM + fl;
+              float r[32];
+              if (staged) {
+                const float* sp = reinterpret_cast<const float*>(tiles) + size_t(idx) * slot_floats + off;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) r[jj] = sp[size_t(jj) * UM];
+              } else {
+                const int slot = ((o * per) / k_iters == t) ? 2 * o : 2 * o + 1;
+                const float* rp = ws + size_t(slot) * slot_floats + off;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) r[jj] = __ldcg(rp + size_t(jj) * UM);
+              }
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) v[jj] += r[jj];
+              ++idx;
+            }
+            const int t0 = x0 + c * 32;
+            if (probe & 128) {  // measurement: no output stores
+              if (v[0] == 12345.f) y[0] = __float2bfloat16(v[1]);
+            } else if (vec_out) {
+              // transpose through shared memory: 4 lanes write one token's
+              // 32 features as 16-byte vectors
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj) stage[jj * 40 + lane] = __float2bfloat16(v[jj] + b);
+              __syncwarp();
+              const int fbase = m0 + i * kGemmBM + q * 32;
+#pragma unroll
+              for (int r0 = 0; r0 < 32; r0 += 8) {
+                const int row = r0 + (lane >> 2), part = lane & 3;
+                const int fo = fbase + part * 8;
+                if (t0 + row < N && fo < M)
+                  *reinterpret_cast<uint4*>(y + int64_t(t0 + row) * ldy + fo) =
+                      *reinterpret_cast<const uint4*>(stage + row * 40 + part * 8);
+              }
+              __syncwarp();
+            } else if (f < M) {
+#pragma unroll
+              for (int jj = 0; jj < 32; ++jj)
+                if (t0 + jj < N) y[int64_t(t0 + jj) * ldy + f] = __float2bfloat16(v[jj] + b);
+            }
+          }
+        }
+      }
+      stamp(3 + 3 * p);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  stamp(15);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(S::TMEM_COLS));
+  }
+}
+
 __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
                                      const float* __restrict__ ws,
                                      const __nv_bfloat16* __restrict__ bias, int M, int N,
@@ -442,6 +834,128 @@ static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloa
   SWIFT_CHECK_LAUNCH();
 }
 
+// ---- stream-K host side
+struct SkBuffers {
+  float* ws = nullptr;
+  int* counters = nullptr;
+  unsigned long long* stamps = nullptr;  // probe 3 timestamps [grid][16]
+};
+constexpr int kSkMaxTiles = 8192;
+constexpr size_t kSkSlotFloats = 256 * 256;  // UM * BN at most
+
+// Per-device workspace (two partial slots per CTA) and zeroed tile counters,
+// allocated once and kept for the process (CUDA graphs capture the pointers).
+static SkBuffers& sk_buffers() {
+  static SkBuffers b[64];
+  int dev;
+  cudaGetDevice(&dev);
+  if (!b[dev].ws) {
+    SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].ws, size_t(2) * num_sms() * kSkSlotFloats * sizeof(float)));
+    SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].counters, kSkMaxTiles * sizeof(int)));
+    SWIFT_CHECK_CUDA(cudaMemset(b[dev].counters, 0, kSkMaxTiles * sizeof(int)));
+    SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].stamps, 256 * 16 * sizeof(unsigned long long)));
+    SWIFT_CHECK_CUDA(cudaMemset(b[dev].stamps, 0, 256 * 16 * sizeof(unsigned long long)));
+    SWIFT_CHECK_CUDA(cudaDeviceSynchronize());
+  }
+  return b[dev];
+}
+
+static int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : dflt;
+}
+
+template <int BN, int MT>
+static void launch_sk(const void* w, int64_t ldw, const void* x, int64_t ldx, __nv_bfloat16* y,
+                      int64_t ldy, const __nv_bfloat16* bias, int M, int N, int K, int grid,
+                      int per, int packed_kt = 0) {
+  // 16-byte output vectors need 8-feature groups that stay inside rows
+  const int vec_out = (M % 8 == 0 && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) ? 1 : 0;
+  constexpr int SB = SkSmem<BN, MT, 1>::STAGE_BYTES;
+  constexpr int STAGES = std::min(8, (200 * 1024) / SB);
+  using S = SkSmem<BN, MT, STAGES>;
+  auto kern = gemm_streamk_kernel<BN, MT, STAGES>;
+  static bool attr[64] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr[dev]) {
+    SWIFT_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(S::BYTES)));
+    attr[dev] = true;
+  }
+  SkBuffers& b = sk_buffers();
+  // packed: [ceil(M/128) * KT * 128 rows, 64 cols], one 128-row box per tile
+  CUtensorMap tw = packed_kt
+                       ? make_tmap(w, int64_t((M + kGemmBM - 1) / kGemmBM) * packed_kt * kGemmBM,
+                                   kGemmBK, kGemmBK, kGemmBM)
+                       : make_tmap(w, M, K, ldw, S::UM);
+  CUtensorMap tx = make_tmap(x, N, K, ldx, BN);
+  kern<<<grid, kGemmThreads, S::BYTES, cur_stream()>>>(tw, tx, y, ldy, bias, b.ws, b.counters, M,
+                                                       N, K, per, status_word_ptr(),
+                                                       env_int("SWIFT_SK_PROBE", 0), vec_out,
+                                                       b.stamps, packed_kt,
+                                                       env_int("SWIFT_SK_ROT", 0));
+  SWIFT_CHECK_LAUNCH();
+}
+
+
+// Stream-K plan for tokens N <= 256: token tile BN (one tile), MT x 128
+// features per unit, grid and iterations per CTA. false: not applicable.
+static void plan(int M, int N, int K, int* bn, int* splits);
+
+// Stream-K for decode-shaped GEMMs (N <= 256 tokens; SWIFT_GEMM_STREAMK=0
+// turns it off). Token tile: the smallest power of two >= N (>= 32), halved
+// from 256 to 128 while the feature tiles x 2 still fit two waves (measured
+// on B200 for the Llama-2-7B projections: the narrower tile halves the
+// partial-sum traffic, which outweighs the second read of each weight tile,
+// served from L2). At least 32 k-iterations per CTA.
+static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per) {
+  const int mode = env_int("SWIFT_GEMM_STREAMK", 1);
+  if (N > 256 || mode == 0) return false;
+  const int sms = num_sms();
+  int b = 32;
+  while (b < N) b *= 2;
+  if (b == 256 && int64_t((M + kGemmBM - 1) / kGemmBM) * 2 <= int64_t(2) * sms) b = 128;
+  const int bo = env_int("SWIFT_SK_BN", 0);  // tuning override: narrower token tiles
+  if (bo == 32 || bo == 64 || bo == 128) b = std::min(b, bo);
+  const int k_iters = (K + kGemmBK - 1) / kGemmBK;
+  int m = env_int("SWIFT_SK_MT", 0);
+  if (m != 1 && m != 2) m = 1;
+  const int units = (M + 128 * m - 1) / (128 * m) * ((N + b - 1) / b);
+  if (units > kSkMaxTiles) return false;
+  const int64_t total = int64_t(units) * k_iters;
+  const int min_per = std::max(1, env_int("SWIFT_SK_MINPER", 32));
+  int g = static_cast<int>(std::min<int64_t>(sms, (total + min_per - 1) / min_per));
+  g = std::max(g, 1);
+  int p = static_cast<int>((total + g - 1) / g);
+  g = static_cast<int>((total + p - 1) / p);
+  *bn = b;
+  *mt = m;
+  *grid = g;
+  *per = p;
+  return true;
+}
+
+static bool gemm_streamk(torch::Tensor out, torch::Tensor x, torch::Tensor w,
+                         const __nv_bfloat16* bias, int64_t T, int64_t ldx, int64_t ldy,
+                         int Mp = 0, int packed_kt = 0) {
+  const int M = packed_kt ? Mp : static_cast<int>(w.size(0));
+  const int K = static_cast<int>(x.size(-1));
+  const int N = static_cast<int>(T);
+  int bn, mt, grid, per;
+  if (!sk_plan(M, N, K, &bn, &mt, &grid, &per)) return false;
+  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+  const void* wp = w.data_ptr();
+  const void* xp = x.data_ptr();
+  const int64_t ldw = w.stride(0);
+#define SK_CASE(B, MTV) \
+  if (bn == B && mt == MTV) { launch_sk<B, MTV>(wp, ldw, xp, ldx, y, ldy, bias, M, N, K, grid, per, packed_kt); return true; }
+  SK_CASE(32, 1) SK_CASE(32, 2) SK_CASE(64, 1) SK_CASE(64, 2)
+  SK_CASE(128, 1) SK_CASE(128, 2) SK_CASE(256, 1) SK_CASE(256, 2)
+#undef SK_CASE
+  return false;
+}
+
 // Token-tile width and split count for a (features M, tokens N, K) problem.
 static void plan(int M, int N, int K, int* bn, int* splits) {
   const int sms = num_sms();
@@ -484,6 +998,12 @@ int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<
                   reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
               "gemm: operands must be 16-byte aligned");
   if (T == 0) return 0;
+  {
+    const __nv_bfloat16* bsk =
+        bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
+                         : nullptr;
+    if (gemm_streamk(out, x, w, bsk, T, ldx, ldy)) return 1;
+  }
   int bn, splits;
   plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);
   CUtensorMap tw = make_tmap(w.data_ptr(), M, K, w.stride(0), kGemmBM);
@@ -516,10 +1036,48 @@ int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<
   return 1;
 }
 
+// Weights in tile-packed order: w_packed [ceil(M/128), ceil(K/64), 128, 64]
+// (zero padded), so every 128 x 64 weight tile is one contiguous 16 KB block.
+// Decode-shaped only (tokens <= 256). out [T, M], x [T, K].
+int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
+                    c10::optional<torch::Tensor> bias) {
+  CHECK_BF16(x);
+  CHECK_BF16(wp);
+  CHECK_BF16(out);
+  TORCH_CHECK(wp.dim() == 4 && wp.size(2) == kGemmBM && wp.size(3) == kGemmBK && wp.is_contiguous());
+  const int64_t K = x.size(-1), T = x.numel() / K;
+  TORCH_CHECK(wp.size(0) == (M + kGemmBM - 1) / kGemmBM && wp.size(1) == (K + kGemmBK - 1) / kGemmBK);
+  TORCH_CHECK(T <= 256, "gemm_packed: at most 256 tokens");
+  if (T == 0) return 0;
+  const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
+  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M;
+  const __nv_bfloat16* bp =
+      bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
+                       : nullptr;
+  TORCH_CHECK(gemm_streamk(out, x, wp, bp, T, ldx, ldy, static_cast<int>(M),
+                           static_cast<int>(wp.size(1))),
+              "gemm_packed: no stream-K plan");
+  return 1;
+}
+
+// Timestamps of the last stream-K launch made with SWIFT_SK_PROBE bit 4 set
+// ([256, 16] int64 nanoseconds; 0 = not reached), for kernel phase timing.
+torch::Tensor gemm_sk_stamps() {
+  SkBuffers& b = sk_buffers();
+  auto t = torch::empty({256, 16}, torch::dtype(torch::kInt64));
+  SWIFT_CHECK_CUDA(cudaMemcpy(t.data_ptr(), b.stamps, 256 * 16 * 8, cudaMemcpyDeviceToHost));
+  SWIFT_CHECK_CUDA(cudaMemset(b.stamps, 0, 256 * 16 * 8));
+  return t;
+}
+
+// [token tile, splits, stream-K features-per-unit / 128 (0: not stream-K),
+//  grid, k-iterations per CTA]
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K) {
-  int bn, s;
+  int bn, s, mt, grid, per;
+  if (sk_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), &bn, &mt, &grid, &per))
+    return {bn, 1, mt, grid, per};
   plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), &bn, &s);
-  return {bn, s};
+  return {bn, s, 0, 0, 0};
 }
 
 }  // namespace swift

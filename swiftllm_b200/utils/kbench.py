@@ -5,8 +5,9 @@ single-shot runners used for ncu captures.
   python -m swiftllm_b200.utils.kbench decode --shape 256,900,32,32 [--splits 1] [--once]
   python -m swiftllm_b200.utils.kbench prefill --shape 8,1024,32,8
   python -m swiftllm_b200.utils.kbench sweep [--json out.json]
+  python -m swiftllm_b200.utils.kbench step --shape 256,700 [--model llama-2-7b] [--eager] [--once]
 
-Timing rule: 3 warm-up runs, then each timed run writes a 256 MB buffer
+Timing rule: 3 warm-up runs, then each timed run reads a 256 MB buffer
 (larger than the 126 MB L2) before it, is bracketed by CUDA events on the
 current stream with synchronisation on both sides; the median is reported.
 Bandwidth / FLOP rates are also given as fractions of MEASURED_PEAKS.json.
@@ -18,6 +19,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 import sys
 
 import torch
@@ -26,13 +28,22 @@ from ..ops import cuda_ext
 from .timing import measured_peaks
 
 
-def _time(fn, iters=20):
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+def _time(fn, iters=20, flush=True):
+    # flush = READ a 256 MB buffer (L2 left full of clean lines). Writing it
+    # instead would leave ~126 MB of dirty lines whose write-back lands inside
+    # the timed kernel; SWIFT_KBENCH_FLUSH=write selects that variant.
+    buf = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    sink = torch.empty((), dtype=torch.float32, device="cuda")
+    write = os.environ.get("SWIFT_KBENCH_FLUSH", "read") == "write"
     for _ in range(3):
         fn()
     ts = []
     for _ in range(iters):
-        flush.zero_()
+        if flush:
+            if write:
+                buf.zero_()
+            else:
+                torch.sum(buf, dim=0, out=sink)
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda.synchronize()
         s.record()
@@ -115,6 +126,194 @@ def prefill_case(S, L, Hq, Hkv, once=False, D=128):
             "TFLOP/s": round(fl / ms / 1e9, 1), "frac_flops": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
 
 
+def step_case(S, ctx, model="llama-2-7b", eager=False, once=False, iters=20):
+    """One decode step of the whole model (S sequences at context ctx):
+    the engine's ModelRunner with random-init weights, CUDA-graph replay
+    unless eager. Reports ms per step and output tokens/s."""
+    import numpy as np
+    from ..config import EngineConfig
+    from ..models.config import load_config
+    from ..runtime.model_runner import ModelRunner, StepInput
+    mcfg = load_config(model)
+    bs = 16
+    nbp = (ctx + 1 + bs - 1) // bs
+    ec = EngineConfig(model=model, load_format="dummy", dtype="bfloat16", max_model_len=2048,
+                      max_num_seqs=max(S, 1), enforce_eager=eager, max_num_batched_tokens=S)
+    r = ModelRunner(mcfg, ec, torch.device("cuda", torch.cuda.current_device()), max_model_len=2048)
+    r.load_weights()
+    r.allocate_kv(S * nbp + 1, 0)
+    r.capture_graphs(S)
+    tables = np.arange(S * nbp, dtype=np.int32).reshape(S, nbp)
+    pos = np.full(S, ctx, dtype=np.int32)
+    slots = (tables[:, ctx // bs] * bs + ctx % bs).astype(np.int32)
+    ids = np.random.default_rng(0).integers(0, mcfg.vocab_size, S).astype(np.int32)
+    ints = np.concatenate([ids, pos, slots, np.arange(S + 1, dtype=np.int32), pos + 1,
+                           tables.reshape(-1)]).astype(np.int32)
+    e2 = np.zeros((0, 2), np.int64)
+    si = StepInput(S, S, S, 1, ctx + 1, nbp, ints, np.arange(S, dtype=np.int32), e2, e2, e2)
+    fn = lambda: r.execute(si)  # noqa: E731
+    if once:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {}
+    for _ in range(3):
+        fn()
+    ts = []
+    for _ in range(iters):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    ms = ts[len(ts) // 2]
+    kv = S * (ctx + 1) * mcfg.num_layers * 2 * mcfg.num_kv_heads * mcfg.head_dim * 2
+    w = sum(p.numel() for _, p in r.model.named_parameters()) * 2
+    pk = measured_peaks()
+    return {"op": "decode_step", "model": model, "S": S, "ctx": ctx, "graphs": not eager,
+            "ms": round(ms, 3), "tok/s": round(S / ms * 1e3, 1), "weights_GB": round(w / 1e9, 2),
+            "kv_GB": round(kv / 1e9, 2), "frac_bw": round((w + kv) / ms / 1e9 / (pk["hbm_gbs"] / 1e3), 3)}
+
+
+def sk_sweep(T=256):
+    """Stream-K decode GEMM settings (features per unit, minimum k-iterations
+    per CTA) for the Llama-2-7B projections; plus the data-parallel kernel
+    (SWIFT_GEMM_STREAMK=0) and cuBLAS for comparison."""
+    import os
+    res = []
+    for N, K in [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008), (32000, 4096)]:
+        os.environ["SWIFT_GEMM_STREAMK"] = "0"
+        base = gemm_case(T, N, K)
+        os.environ["SWIFT_GEMM_STREAMK"] = "2"
+        best = None
+        for bn in (64, 128, 256):
+            for mp in (8, 32, 128):
+                os.environ["SWIFT_SK_MT"] = "1"
+                os.environ["SWIFT_SK_BN"] = str(bn)
+                os.environ["SWIFT_SK_MINPER"] = str(mp)
+                r = gemm_case(T, N, K, cublas=False)
+                r["mt"], r["minper"], r["bn"] = 1, mp, bn
+                print(json.dumps(r), flush=True)
+                if best is None or r["ms"] < best["ms"]:
+                    best = r
+        for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_GEMM_STREAMK", "SWIFT_SK_BN"):
+            os.environ.pop(k, None)
+        dflt = gemm_case(T, N, K, cublas=False)
+        out = {"N": N, "K": K, "T": T, "dp_ms": base["ms"], "cublas_ms": base["cublas_ms"],
+               "sk_default_ms": dflt["ms"], "sk_default_plan": dflt["plan"],
+               "sk_best_ms": best["ms"], "sk_best": [best["bn"], best["minper"]],
+               "sk_best_TB/s": best["TB/s"], "sk_best_frac_bw": best["frac_bw"]}
+        print(json.dumps(out), flush=True)
+        res.append(out)
+    return res
+
+
+def sk_probe(T=256):
+    """Load-only (probe 1) and MMA-only (probe 2) timings of the stream-K
+    kernel next to the full kernel (probe 0): which side bounds it."""
+    import os
+    res = []
+    for N, K in [(12288, 4096), (4096, 11008)]:
+        for mt in (1,):
+            for probe in (0, 2, 64, 66, 130, 194):
+                os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": "16",
+                                   "SWIFT_SK_PROBE": str(probe), "SWIFT_GEMM_STREAMK": "2"})
+                r = gemm_case(T, N, K, cublas=False)
+                r.update(mt=mt, probe=probe)
+                print(json.dumps(r), flush=True)
+                res.append(r)
+    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_SK_PROBE"):
+        os.environ.pop(k, None)
+    return res
+
+
+def sk_stamps(T=256, N=12288, K=4096, mt=1, minper=16, probe=0):
+    """Phase timing of one stream-K launch (SWIFT_SK_PROBE bit 4): per CTA, the
+    %globaltimer stamps relative to the earliest kernel start, as
+    percentiles over CTAs (microseconds)."""
+    import os
+    import numpy as np
+    os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": str(minper),
+                       "SWIFT_SK_PROBE": str(4 | probe), "SWIFT_GEMM_STREAMK": "2"})
+    C = cuda_ext()
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
+    for _ in range(3):
+        C.gemm(y, x, w, None)
+    flush.sum()
+    torch.cuda.synchronize()
+    C.gemm_sk_stamps()
+    C.gemm(y, x, w, None)
+    torch.cuda.synchronize()
+    st = C.gemm_sk_stamps().numpy().astype(np.float64)
+    plan = C.gemm_plan(N, T, K)
+    g = int(plan[3])
+    st = st[:g]
+    t0 = st[:, 0].min()
+    names = ["start", "s0_ready", "s0_partial", "s0_done", "s1_ready", "s1_partial", "s1_done",
+             "s2_ready", "s2_partial", "s2_done"]
+    out = {"plan": plan, "probe": probe, "rot": os.environ.get("SWIFT_SK_ROT", "0")}
+    for k, nm in enumerate(names):
+        col = st[:, k]
+        col = col[col > 0]
+        if col.size:
+            rel = (col - t0) / 1e3
+            out[nm] = [round(float(np.percentile(rel, p)), 2) for p in (0, 50, 100)]
+    end = (st[:, 15] - t0) / 1e3
+    out["end"] = [round(float(np.percentile(end, p)), 2) for p in (0, 50, 100)]
+    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_SK_PROBE"):
+        os.environ.pop(k, None)
+    print(json.dumps(out), flush=True)
+    return out
+
+
+def pack_weight(w):
+    """[M, K] -> tile-packed [ceil(M/128), ceil(K/64), 128, 64], zero padded."""
+    M, K = w.shape
+    Mp, Kp = (M + 127) // 128 * 128, (K + 63) // 64 * 64
+    wp = torch.zeros(Mp, Kp, dtype=w.dtype, device=w.device)
+    wp[:M, :K] = w
+    return wp.view(Mp // 128, 128, Kp // 64, 64).permute(0, 2, 1, 3).contiguous()
+
+
+def pack_test(T=256):
+    """Row-major vs tile-packed weights in the stream-K kernel, with and
+    without an L2 flush between runs (is the weight stream DRAM-locality
+    bound?)."""
+    import os
+    C = cuda_ext()
+    res = []
+    for N, K in [(12288, 4096), (22016, 4096), (4096, 11008), (4096, 4096)]:
+        x = torch.randn(T, K, device="cuda").bfloat16()
+        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        wp = pack_weight(w)
+        y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+        y2 = torch.empty_like(y)
+        for mt in (1, 2):
+            for mp in (8, 16):
+                os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": str(mp),
+                                   "SWIFT_GEMM_STREAMK": "2"})
+                C.gemm(y, x, w, None)
+                C.gemm_packed(y2, x, wp, N, None)
+                torch.cuda.synchronize()
+                assert torch.equal(y, y2)
+                r = {"N": N, "K": K, "mt": mt, "minper": mp,
+                     "rowmajor_ms": round(_time(lambda: C.gemm(y, x, w, None)), 4),
+                     "packed_ms": round(_time(lambda: C.gemm_packed(y2, x, wp, N, None)), 4),
+                     "rowmajor_l2hot_ms": round(_time(lambda: C.gemm(y, x, w, None), flush=False), 4),
+                     "packed_l2hot_ms": round(_time(lambda: C.gemm_packed(y2, x, wp, N, None), flush=False), 4)}
+                print(json.dumps(r), flush=True)
+                res.append(r)
+    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER"):
+        os.environ.pop(k, None)
+    return res
+
+
 def sweep():
     res = []
     for T, N, K in [(256, 12288, 4096), (256, 4096, 4096), (256, 22016, 4096), (256, 4096, 11008),
@@ -133,7 +332,9 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep"])
+    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest"])
+    ap.add_argument("--model", default="llama-2-7b")
+    ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
     ap.add_argument("--splits", type=int, default=1)
     ap.add_argument("--once", action="store_true")
@@ -141,10 +342,21 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.op == "sweep":
         res = sweep()
+    elif a.op == "skstamps":
+        shp = [int(v) for v in (a.shape or "256,12288,4096,1,16").split(",")]
+        res = sk_stamps(*shp)
+    elif a.op == "packtest":
+        res = pack_test()
+    elif a.op == "skprobe":
+        res = sk_probe()
+    elif a.op == "sksweep":
+        res = sk_sweep(int(a.shape) if a.shape else 256)
     else:
         shp = [int(v) for v in a.shape.split(",")]
         if a.op == "gemm":
             res = gemm_case(*shp, once=a.once)
+        elif a.op == "step":
+            res = step_case(*shp, model=a.model, eager=a.eager, once=a.once)
         elif a.op == "decode":
             res = decode_case(*shp, splits=a.splits, once=a.once)
         else:

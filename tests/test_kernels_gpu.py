@@ -181,6 +181,28 @@ def test_gemm(C, T, N, K):
     _status_ok(C)
 
 
+@pytest.mark.parametrize("mt,minper", [(1, 8), (2, 8), (1, 1), (2, 3)])
+@pytest.mark.parametrize("T,N,K", [(5, 640, 200), (100, 4096, 4096), (256, 12288, 4096),
+                                   (64, 384, 11008), (200, 32000, 1024)])
+def test_gemm_streamk(C, monkeypatch, mt, minper, T, N, K):
+    # stream-K decode path: forced unit height and tiny per-CTA ranges so
+    # tiles are split across many CTAs (partials + last-arriver fix-up)
+    monkeypatch.setenv("SWIFT_GEMM_STREAMK", "2")
+    monkeypatch.setenv("SWIFT_SK_MT", str(mt))
+    monkeypatch.setenv("SWIFT_SK_MINPER", str(minper))
+    plan = C.gemm_plan(N, T, K)
+    assert plan[2] == mt
+    x, w, b = bf(T, K, scale=0.5), bf(N, K, scale=0.05), bf(N)
+    big = torch.zeros(T, N + 64, dtype=torch.bfloat16, device="cuda")
+    out = big[:, 32:32 + N]
+    for _ in range(2):  # second launch reuses the self-resetting tile counters
+        C.gemm(out, x, w, b)
+        r = x.float() @ w.float().t() + b.float()
+        torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=2e-2 * math.sqrt(K / 64) * 0.5)
+    assert big[:, :32].abs().sum() == 0 and big[:, 32 + N:].abs().sum() == 0
+    _status_ok(C)
+
+
 def test_gemm_bias_and_strided_out(C):
     x, w, b = bf(40, 512), bf(384, 512, scale=0.05), bf(384)
     big = torch.zeros(40, 1024, dtype=torch.bfloat16, device="cuda")
