@@ -103,6 +103,86 @@ class ClockSampler:
         return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class HostProfile:
+    """Diagnostic: wraps the engine's executor / sampler / scheduler calls
+    with host timers, and records CUDA events at the start of each step's
+    forward and after its sampling, so the GPU idle gap between steps (host
+    work the GPU waits for) can be measured. Not used for the reported
+    numbers."""
+
+    def __init__(self, eng):
+        import torch
+        self.torch = torch
+        self.t = {"schedule": 0.0, "execute_host": 0.0, "sample_host": 0.0, "update": 0.0,
+                  "process": 0.0}
+        self.n = 0
+        self.ev = []  # (start_event, end_event) per step
+        ex, sm, sch = eng.executor, eng.sampler, eng.scheduler
+        orig_exec, orig_samp = ex.execute, sm.__call__
+        orig_sched, orig_upd = sch.schedule, sch.update
+        orig_proc = eng._process
+        prof = self
+
+        def execute(si):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            t0 = time.perf_counter()
+            out = orig_exec(si)
+            prof.t["execute_host"] += time.perf_counter() - t0
+            prof._start = e0
+            return out
+
+        class _S:
+            def __call__(self_, *a, **k):
+                t0 = time.perf_counter()
+                out = orig_samp(*a, **k)
+                prof.t["sample_host"] += time.perf_counter() - t0
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record()
+                prof.ev.append((prof._start, e1))
+                prof.n += 1
+                return out
+
+            def __getattr__(self_, k):
+                return getattr(sm, k)
+
+        def timed(name, fn):
+            def w(*a, **k):
+                t0 = time.perf_counter()
+                r = fn(*a, **k)
+                prof.t[name] += time.perf_counter() - t0
+                return r
+            return w
+
+        ex.execute = execute
+        eng.sampler = _S()
+        eng.scheduler = _Wrap(sch, schedule=timed("schedule", orig_sched),
+                              update=timed("update", orig_upd))
+        eng._process = timed("process", orig_proc)
+
+    def report(self):
+        self.torch.cuda.synchronize()
+        gaps, busy = [], []
+        for i, (s, e) in enumerate(self.ev):
+            busy.append(s.elapsed_time(e))
+            if i + 1 < len(self.ev):
+                gaps.append(e.elapsed_time(self.ev[i + 1][0]))
+        n = max(self.n, 1)
+        return {"steps": self.n,
+                "host_ms_per_step": {k: round(v / n * 1e3, 3) for k, v in self.t.items()},
+                "gpu_step_ms_avg": round(sum(busy) / max(len(busy), 1), 3),
+                "gpu_idle_gap_ms_avg": round(sum(gaps) / max(len(gaps), 1), 3)}
+
+
+class _Wrap:
+    def __init__(self, obj, **over):
+        self._o = obj
+        self.__dict__.update(over)
+
+    def __getattr__(self, k):
+        return getattr(self._o, k)
+
+
 def reference_arm(args) -> None:
     msg = ("reference cannot be installed or run: its pyproject needs the maturin (Rust) build "
            "backend, absent offline, and its forward pass returns zeros / canned text "
@@ -122,6 +202,8 @@ def main() -> None:
     ap.add_argument("--max-num-seqs", type=int, default=256)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
+    ap.add_argument("--profile-host", action="store_true",
+                    help="report host phases and the GPU idle gap between steps (diagnostic)")
     args = ap.parse_args()
     if args.impl == "reference":
         reference_arm(args)
@@ -174,6 +256,7 @@ def main() -> None:
                 st["launches"] = ops.LAUNCHES[0] - st["launch0"]
 
     eng.step_hook = hook
+    prof = HostProfile(eng) if args.profile_host else None
     torch.cuda.synchronize()
     io_before = list(eng.io_bytes)
     steps_before = eng.num_steps
@@ -232,6 +315,8 @@ def main() -> None:
         "clocks": clk,
         "init_s": round(init_s, 1),
     }
+    if prof is not None:
+        res["host_profile"] = prof.report()
     print(json.dumps(res), flush=True)
     llm.shutdown()
 

@@ -903,19 +903,34 @@ static void launch_sk(const void* w, int64_t ldw, const void* x, int64_t ldx, __
 // features per unit, grid and iterations per CTA. false: not applicable.
 static void plan(int M, int N, int K, int* bn, int* splits);
 
-// Stream-K for decode-shaped GEMMs (N <= 256 tokens; SWIFT_GEMM_STREAMK=0
-// turns it off). Token tile: the smallest power of two >= N (>= 32), halved
+// Stream-K for decode-shaped GEMMs (N <= 256 tokens, and mixed steps of up
+// to 2048 tokens where the rule below says so; SWIFT_GEMM_STREAMK=0 turns it
+// off, 2 forces it). Token tile: the smallest power of two >= N (>= 32), halved
 // from 256 to 128 while the feature tiles x 2 still fit two waves (measured
 // on B200 for the Llama-2-7B projections: the narrower tile halves the
 // partial-sum traffic, which outweighs the second read of each weight tile,
 // served from L2). At least 32 k-iterations per CTA.
 static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per) {
   const int mode = env_int("SWIFT_GEMM_STREAMK", 1);
-  if (N > 256 || mode == 0) return false;
+  if (N > 2048 || mode == 0) return false;
   const int sms = num_sms();
+  if (mode == 1 && N > 256) {
+    // more tokens: stream-K only where the data-parallel plan would split K
+    // or, up to 512 tokens, has few feature tiles (measured on B200)
+    int dbn, dsplits;
+    plan(M, N, K, &dbn, &dsplits);
+    const int m_tiles = (M + kGemmBM - 1) / kGemmBM;
+    if (!(dsplits > 1 || (N <= 512 && m_tiles <= 96))) return false;
+  }
   int b = 32;
-  while (b < N) b *= 2;
-  if (b == 256 && int64_t((M + kGemmBM - 1) / kGemmBM) * 2 <= int64_t(2) * sms) b = 128;
+  while (b < N && b < 256) b *= 2;
+  if (N > 256) {
+    // several token tiles: the width (128 or 256) that pads N the least
+    const int pad128 = (N + 127) / 128 * 128 - N, pad256 = (N + 255) / 256 * 256 - N;
+    b = pad128 < pad256 ? 128 : 256;
+  } else if (b == 256 && int64_t((M + kGemmBM - 1) / kGemmBM) * 2 <= int64_t(2) * sms) {
+    b = 128;
+  }
   const int bo = env_int("SWIFT_SK_BN", 0);  // tuning override: narrower token tiles
   if (bo == 32 || bo == 64 || bo == 128) b = std::min(b, bo);
   const int k_iters = (K + kGemmBK - 1) / kGemmBK;

@@ -314,6 +314,25 @@ def pack_test(T=256):
     return res
 
 
+def mixed_sweep():
+    """Mixed prefill + decode token counts: data-parallel plan vs stream-K."""
+    import os
+    res = []
+    for T in (300, 626, 1000, 1500):
+        for N, K in [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008)]:
+            os.environ["SWIFT_GEMM_STREAMK"] = "0"
+            dp = gemm_case(T, N, K, cublas=True)
+            os.environ["SWIFT_GEMM_STREAMK"] = "2"
+            sk = gemm_case(T, N, K, cublas=False)
+            r = {"T": T, "N": N, "K": K, "dp_ms": dp["ms"], "sk_ms": sk["ms"],
+                 "cublas_ms": dp["cublas_ms"], "sk_plan": sk["plan"], "dp_plan": dp["plan"]}
+            print(json.dumps(r), flush=True)
+            res.append(r)
+    for k in ("SWIFT_GEMM_STREAMK",):
+        os.environ.pop(k, None)
+    return res
+
+
 def sweep():
     res = []
     for T, N, K in [(256, 12288, 4096), (256, 4096, 4096), (256, 22016, 4096), (256, 4096, 11008),
@@ -332,7 +351,7 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest"])
+    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest", "mixed"])
     ap.add_argument("--model", default="llama-2-7b")
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
@@ -345,6 +364,8 @@ def main(argv=None):
     elif a.op == "skstamps":
         shp = [int(v) for v in (a.shape or "256,12288,4096,1,16").split(",")]
         res = sk_stamps(*shp)
+    elif a.op == "mixed":
+        res = mixed_sweep()
     elif a.op == "packtest":
         res = pack_test()
     elif a.op == "skprobe":

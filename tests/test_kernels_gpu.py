@@ -183,7 +183,8 @@ def test_gemm(C, T, N, K):
 
 @pytest.mark.parametrize("mt,minper", [(1, 8), (2, 8), (1, 1), (2, 3)])
 @pytest.mark.parametrize("T,N,K", [(5, 640, 200), (100, 4096, 4096), (256, 12288, 4096),
-                                   (64, 384, 11008), (200, 32000, 1024)])
+                                   (64, 384, 11008), (200, 32000, 1024), (600, 1000, 640),
+                                   (1000, 2048, 1024)])
 def test_gemm_streamk(C, monkeypatch, mt, minper, T, N, K):
     # stream-K decode path: forced unit height and tiny per-CTA ranges so
     # tiles are split across many CTAs (partials + last-arriver fix-up)
