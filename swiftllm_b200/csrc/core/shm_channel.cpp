@@ -110,9 +110,12 @@ class ShmChannel {
 
   void beat() { hdr_->heartbeat_ns[owner_ ? 0 : reader_ + 1].store(now_ns(), std::memory_order_relaxed); }
 
-  // Seconds since the given party last stamped its heartbeat (party 0 = writer).
+  // Seconds since the given party last stamped its heartbeat (party 0 =
+  // writer); -1 if it never has (a worker still loading its weights).
   double heartbeat_age(int party) const {
-    return (now_ns() - hdr_->heartbeat_ns[party].load(std::memory_order_relaxed)) * 1e-9;
+    const int64_t t = hdr_->heartbeat_ns[party].load(std::memory_order_relaxed);
+    if (t == 0) return -1.0;
+    return (now_ns() - t) * 1e-9;
   }
 
   void publish(const char* data, size_t len, double timeout) {

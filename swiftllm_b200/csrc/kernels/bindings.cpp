@@ -33,6 +33,12 @@ void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
 torch::Tensor gemm_sk_stamps();
+int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t s_max,
+                int64_t flag_off, torch::Tensor ctr);
+void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
+                  int64_t s_max, int64_t T, int64_t H, int64_t flag_off, torch::Tensor gemm_epochs,
+                  torch::Tensor epochs, double timeout_s);
 int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
                     c10::optional<torch::Tensor> bias);
 void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
@@ -67,6 +73,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &swift::gemm_plan);
   m.def("gemm_sk_stamps", &swift::gemm_sk_stamps);
   m.def("gemm_packed", &swift::gemm_packed);
+  m.def("gemm_rs", &swift::gemm_rs);
+  m.def("tp_rs_finish", &swift::tp_rs_finish);
   m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
   m.def("gemm_grouped", &swift::gemm_grouped);

@@ -128,6 +128,71 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ---- fused GEMM -> reduce-scatter over NVLink (tensor parallelism)
+// When k > 0 the epilogue does not store into `y`: output row t (a token) is
+// stored straight into the symmetric receive buffer of the rank that owns
+// that token, at [src = this rank][t - lo(owner)][:], with plain stores
+// through the peer mapping (NVLink). Token ownership is contiguous:
+// lo(j) = T*j/k. After the last CTA has finished, the kernel publishes its
+// completion epoch to every peer's flag slot (st.release.sys), and
+// tp_rs_finish (tp_allreduce.cu) reduces each rank's own tokens.
+struct ScatterDesc {
+  uint64_t base[8];   // symmetric allocation of every rank (byte address)
+  int64_t in_off;     // byte offset of this call's receive buffer
+  int64_t flag_off;   // byte offset of the [src rank] u32 completion flags
+  uint32_t* ctr;      // this rank's device counters: [0] epoch, [2] CTA done count
+  int k, rank, s_max, T, H;
+};
+
+__device__ __forceinline__ int sc_owner(const ScatterDesc& sc, int t) {
+  return static_cast<int>((int64_t(t + 1) * sc.k - 1) / sc.T);
+}
+// row base pointer of output row t
+__device__ __forceinline__ __nv_bfloat16* sc_row(const ScatterDesc& sc, __nv_bfloat16* y,
+                                                 int64_t ldy, int t) {
+  if (sc.k == 0) return y + int64_t(t) * ldy;
+  const int j = sc_owner(sc, t);
+  const int lo = static_cast<int>(int64_t(sc.T) * j / sc.k);
+  return reinterpret_cast<__nv_bfloat16*>(sc.base[j] + sc.in_off) +
+         (int64_t(sc.rank) * sc.s_max + (t - lo)) * sc.H;
+}
+// Rows t0 .. t0+n-1 as base + j*stride when they share an owner (else null).
+__device__ __forceinline__ __nv_bfloat16* sc_run(const ScatterDesc& sc, __nv_bfloat16* y,
+                                                 int64_t ldy, int t0, int n, int64_t* stride) {
+  if (sc.k == 0) {
+    *stride = ldy;
+    return y + int64_t(t0) * ldy;
+  }
+  *stride = sc.H;
+  const int last = min(t0 + n - 1, sc.T - 1);
+  if (t0 >= sc.T || sc_owner(sc, t0) != sc_owner(sc, last)) return nullptr;
+  return sc_row(sc, y, ldy, t0);
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// End of a fused GEMM (all threads, after the CTA's final __syncthreads):
+// the last CTA to finish bumps the epoch and publishes it to every rank.
+__device__ __forceinline__ void sc_publish(const ScatterDesc& sc) {
+  if (sc.k == 0) return;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t old = atomicAdd(&sc.ctr[2], 1u);
+    if (old == gridDim.x - 1) {
+      __threadfence_system();
+      sc.ctr[2] = 0;
+      const uint32_t ep = sc.ctr[0] + 1;
+      sc.ctr[0] = ep;
+      for (int r = 0; r < sc.k; ++r)
+        st_release_sys_u32(reinterpret_cast<uint32_t*>(sc.base[r] + sc.flag_off) + sc.rank, ep);
+    }
+  }
+}
+
 template <int BN, int STAGES>
 struct GemmSmem {
   static constexpr int A_BYTES = kGemmBM * kGemmBK * 2;
@@ -147,7 +212,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
                         int64_t ldy, const __nv_bfloat16* __restrict__ bias,
                         float* __restrict__ ws, int M, int N, int K, int splits, int* status,
-                        const int32_t* __restrict__ goff, int groups) {
+                        const int32_t* __restrict__ goff, int groups, const ScatterDesc sc) {
   using S = GemmSmem<BN, STAGES>;
   // Grouped mode (goff != nullptr, MoE experts): group g multiplies the token
   // rows [goff[g], goff[g+1]) by weight rows [g*M, (g+1)*M); tiles never
@@ -332,9 +397,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int t0 = x0 + c * 32;
           if (f < M) {
             if (splits == 1) {
+              int64_t rs;
+              __nv_bfloat16* run = sc_run(sc, y, ldy, t0, 32, &rs);
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (t0 + j < xend) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+                if (t0 + j < xend)
+                  (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(v[j] + b);
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
@@ -348,9 +416,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int t0 = x0;
         if (f < M) {
           if (splits == 1) {
+            int64_t rs;
+            __nv_bfloat16* run = sc_run(sc, y, ldy, t0, 16, &rs);
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (t0 + j < xend) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+              if (t0 + j < xend)
+                (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(v[j] + b);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -365,6 +436,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  sc_publish(sc);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -405,7 +477,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         int64_t ldy, const __nv_bfloat16* __restrict__ bias,
                         float* __restrict__ ws, int* __restrict__ counters, int M, int N, int K,
                         int per, int* status, int probe, int vec_out,
-                        unsigned long long* __restrict__ stamps, int packed_kt, int rot_mul) {
+                        unsigned long long* __restrict__ stamps, int packed_kt, int rot_mul,
+                        const ScatterDesc sc) {
   using S = SkSmem<BN, MT, STAGES>;
   constexpr int UM = S::UM, NBUF = S::NBUF;
   extern __shared__ uint8_t smem_raw[];
@@ -728,19 +801,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               for (int jj = 0; jj < 32; ++jj) stage[jj * 40 + lane] = __float2bfloat16(v[jj] + b);
               __syncwarp();
               const int fbase = m0 + i * kGemmBM + q * 32;
+              int64_t rs;
+              __nv_bfloat16* run = sc_run(sc, y, ldy, t0, 32, &rs);
 #pragma unroll
               for (int r0 = 0; r0 < 32; r0 += 8) {
                 const int row = r0 + (lane >> 2), part = lane & 3;
                 const int fo = fbase + part * 8;
                 if (t0 + row < N && fo < M)
-                  *reinterpret_cast<uint4*>(y + int64_t(t0 + row) * ldy + fo) =
+                  *reinterpret_cast<uint4*>((run ? run + row * rs : sc_row(sc, y, ldy, t0 + row)) + fo) =
                       *reinterpret_cast<const uint4*>(stage + row * 40 + part * 8);
               }
               __syncwarp();
             } else if (f < M) {
 #pragma unroll
               for (int jj = 0; jj < 32; ++jj)
-                if (t0 + jj < N) y[int64_t(t0 + jj) * ldy + f] = __float2bfloat16(v[jj] + b);
+                if (t0 + jj < N) sc_row(sc, y, ldy, t0 + jj)[f] = __float2bfloat16(v[jj] + b);
             }
           }
         }
@@ -753,6 +828,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  sc_publish(sc);
   stamp(15);
   if (warp == 1) {
     tc_fence_after();
@@ -815,7 +891,8 @@ static int num_sms() {
 template <int BN, int STAGES>
 static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloat16* y, int64_t ldy,
                         const __nv_bfloat16* bias, float* ws, int M, int N, int K, int splits,
-                        const int32_t* goff = nullptr, int groups = 0) {
+                        const int32_t* goff = nullptr, int groups = 0,
+                        const ScatterDesc& sc = ScatterDesc{}) {
   using S = GemmSmem<BN, STAGES>;
   auto kern = gemm_tcgen05_kernel<BN, STAGES>;
   static bool attr[64] = {false};
@@ -830,7 +907,7 @@ static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloa
   const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN + (goff ? groups : 0)) * splits;
   const int grid = std::min(tiles, num_sms());
   kern<<<grid, kGemmThreads, S::BYTES, cur_stream()>>>(tw, tx, y, ldy, bias, ws, M, N, K, splits,
-                                                       status_word_ptr(), goff, groups);
+                                                       status_word_ptr(), goff, groups, sc);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -868,7 +945,7 @@ static int env_int(const char* name, int dflt) {
 template <int BN, int MT>
 static void launch_sk(const void* w, int64_t ldw, const void* x, int64_t ldx, __nv_bfloat16* y,
                       int64_t ldy, const __nv_bfloat16* bias, int M, int N, int K, int grid,
-                      int per, int packed_kt = 0) {
+                      int per, int packed_kt = 0, const ScatterDesc& sc = ScatterDesc{}) {
   // 16-byte output vectors need 8-feature groups that stay inside rows
   const int vec_out = (M % 8 == 0 && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) ? 1 : 0;
   constexpr int SB = SkSmem<BN, MT, 1>::STAGE_BYTES;
@@ -894,7 +971,7 @@ static void launch_sk(const void* w, int64_t ldw, const void* x, int64_t ldx, __
                                                        N, K, per, status_word_ptr(),
                                                        env_int("SWIFT_SK_PROBE", 0), vec_out,
                                                        b.stamps, packed_kt,
-                                                       env_int("SWIFT_SK_ROT", 0));
+                                                       env_int("SWIFT_SK_ROT", 0), sc);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -910,8 +987,9 @@ static void plan(int M, int N, int K, int* bn, int* splits);
 // on B200 for the Llama-2-7B projections: the narrower tile halves the
 // partial-sum traffic, which outweighs the second read of each weight tile,
 // served from L2). At least 32 k-iterations per CTA.
-static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per) {
-  const int mode = env_int("SWIFT_GEMM_STREAMK", 1);
+static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per,
+                    bool force = false) {
+  const int mode = force ? 2 : env_int("SWIFT_GEMM_STREAMK", 1);
   if (N > 2048 || mode == 0) return false;
   const int sms = num_sms();
   if (mode == 1 && N > 256) {
@@ -951,20 +1029,19 @@ static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per) 
   return true;
 }
 
-static bool gemm_streamk(torch::Tensor out, torch::Tensor x, torch::Tensor w,
+static bool gemm_streamk(__nv_bfloat16* y, torch::Tensor x, torch::Tensor w,
                          const __nv_bfloat16* bias, int64_t T, int64_t ldx, int64_t ldy,
-                         int Mp = 0, int packed_kt = 0) {
+                         int Mp = 0, int packed_kt = 0, const ScatterDesc& sc = ScatterDesc{}) {
   const int M = packed_kt ? Mp : static_cast<int>(w.size(0));
   const int K = static_cast<int>(x.size(-1));
   const int N = static_cast<int>(T);
   int bn, mt, grid, per;
-  if (!sk_plan(M, N, K, &bn, &mt, &grid, &per)) return false;
-  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+  if (!sk_plan(M, N, K, &bn, &mt, &grid, &per, sc.k > 0)) return false;
   const void* wp = w.data_ptr();
   const void* xp = x.data_ptr();
   const int64_t ldw = w.stride(0);
 #define SK_CASE(B, MTV) \
-  if (bn == B && mt == MTV) { launch_sk<B, MTV>(wp, ldw, xp, ldx, y, ldy, bias, M, N, K, grid, per, packed_kt); return true; }
+  if (bn == B && mt == MTV) { launch_sk<B, MTV>(wp, ldw, xp, ldx, y, ldy, bias, M, N, K, grid, per, packed_kt, sc); return true; }
   SK_CASE(32, 1) SK_CASE(32, 2) SK_CASE(64, 1) SK_CASE(64, 2)
   SK_CASE(128, 1) SK_CASE(128, 2) SK_CASE(256, 1) SK_CASE(256, 2)
 #undef SK_CASE
@@ -995,38 +1072,31 @@ static void plan(int M, int N, int K, int* bn, int* splits) {
 // out [T, N] (row stride may exceed N), x [T, K], w [N, K], bias [N] or None.
 // Split-K partials go to `ws` when given (fp32, >= splits*T*N), else to a
 // fresh tensor. Returns the number of kernels launched.
-int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias) {
+static int64_t gemm_impl(__nv_bfloat16* y, int64_t ldy, torch::Tensor x, torch::Tensor w,
+                         c10::optional<torch::Tensor> bias, const ScatterDesc& sc) {
   CHECK_BF16(x);
   CHECK_BF16(w);
-  CHECK_BF16(out);
   const int64_t K = x.size(-1);
   const int64_t T = x.numel() / K;
   const int64_t M = w.size(0);
   TORCH_CHECK(w.size(1) == K, "gemm: K mismatch");
-  TORCH_CHECK(x.stride(-1) == 1 && w.stride(1) == 1 && out.stride(-1) == 1,
-              "gemm: inner dim must be contiguous");
+  TORCH_CHECK(x.stride(-1) == 1 && w.stride(1) == 1, "gemm: inner dim must be contiguous");
   TORCH_CHECK(K % 8 == 0, "gemm: K must be a multiple of 8 (16-byte TMA rows)");
   const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
-  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M;
   TORCH_CHECK(ldx % 8 == 0 && w.stride(0) % 8 == 0, "gemm: row strides must be 16-byte multiples");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
               "gemm: operands must be 16-byte aligned");
   if (T == 0) return 0;
-  {
-    const __nv_bfloat16* bsk =
-        bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
-                         : nullptr;
-    if (gemm_streamk(out, x, w, bsk, T, ldx, ldy)) return 1;
-  }
-  int bn, splits;
-  plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);
-  CUtensorMap tw = make_tmap(w.data_ptr(), M, K, w.stride(0), kGemmBM);
-  CUtensorMap tx = make_tmap(x.data_ptr(), T, K, ldx, bn);
-  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   const __nv_bfloat16* bp =
       bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
                        : nullptr;
+  if (gemm_streamk(y, x, w, bp, T, ldx, ldy, 0, 0, sc)) return 1;
+  int bn, splits;
+  plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);
+  if (sc.k > 0) splits = 1;  // the fused scatter stores final values only
+  CUtensorMap tw = make_tmap(w.data_ptr(), M, K, w.stride(0), kGemmBM);
+  CUtensorMap tx = make_tmap(x.data_ptr(), T, K, ldx, bn);
   torch::Tensor ws;
   float* wsp = nullptr;
   if (splits > 1) {
@@ -1035,11 +1105,11 @@ int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<
   }
   const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K);
   switch (bn) {
-    case 16: launch_gemm<16, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits); break;
-    case 32: launch_gemm<32, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits); break;
-    case 64: launch_gemm<64, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits); break;
-    case 128: launch_gemm<128, 6>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits); break;
-    default: launch_gemm<256, 4>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits); break;
+    case 16: launch_gemm<16, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, sc); break;
+    case 32: launch_gemm<32, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, sc); break;
+    case 64: launch_gemm<64, 8>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, sc); break;
+    case 128: launch_gemm<128, 6>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, sc); break;
+    default: launch_gemm<256, 4>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, sc); break;
   }
   if (splits > 1) {
     int64_t n = M * T;
@@ -1049,6 +1119,42 @@ int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<
     return 2;
   }
   return 1;
+}
+
+int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias) {
+  CHECK_BF16(out);
+  TORCH_CHECK(out.stride(-1) == 1, "gemm: inner dim must be contiguous");
+  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : w.size(0);
+  return gemm_impl(reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), ldy, x, w,
+                   bias, ScatterDesc{});
+}
+
+// Fused GEMM -> reduce-scatter (tensor parallelism): y = x . w^T is not
+// stored locally; each output row goes to the receive buffer of the rank
+// owning that token (see ScatterDesc). `ctr` (int32 [4], this rank) holds
+// the completion epoch and the CTA counter. Returns launches.
+int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+                std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t s_max,
+                int64_t flag_off, torch::Tensor ctr) {
+  const int k = static_cast<int>(bases.size());
+  TORCH_CHECK(k >= 2 && k <= 8, "gemm_rs: 2..8 ranks");
+  TORCH_CHECK(ctr.scalar_type() == at::kInt && ctr.numel() >= 4 && ctr.is_cuda());
+  TORCH_CHECK(in_off % 16 == 0 && flag_off % 4 == 0);
+  const int64_t K = x.size(-1), T = x.numel() / K, H = w.size(0);
+  TORCH_CHECK(H % 8 == 0, "gemm_rs: output width must be a multiple of 8");
+  TORCH_CHECK((T + k - 1) / k <= s_max, "gemm_rs: token shard exceeds the receive slots");
+  ScatterDesc sc{};
+  for (int r = 0; r < 8; ++r) sc.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
+  sc.in_off = in_off;
+  sc.flag_off = flag_off;
+  sc.ctr = reinterpret_cast<uint32_t*>(ctr.data_ptr<int32_t>());
+  sc.k = k;
+  sc.rank = static_cast<int>(rank);
+  sc.s_max = static_cast<int>(s_max);
+  sc.T = static_cast<int>(T);
+  sc.H = static_cast<int>(H);
+  if (T == 0) return 0;
+  return gemm_impl(nullptr, 0, x, w, bias, sc);
 }
 
 // Weights in tile-packed order: w_packed [ceil(M/128), ceil(K/64), 128, 64]
@@ -1069,8 +1175,8 @@ int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_
   const __nv_bfloat16* bp =
       bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
                        : nullptr;
-  TORCH_CHECK(gemm_streamk(out, x, wp, bp, T, ldx, ldy, static_cast<int>(M),
-                           static_cast<int>(wp.size(1))),
+  TORCH_CHECK(gemm_streamk(reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), x, wp,
+                           bp, T, ldx, ldy, static_cast<int>(M), static_cast<int>(wp.size(1))),
               "gemm_packed: no stream-K plan");
   return 1;
 }

@@ -146,6 +146,94 @@ void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, i
   SWIFT_CHECK_LAUNCH();
 }
 
+// Second half of the fused GEMM -> all-reduce. gemm_rs has stored every
+// rank's partial rows of this rank's tokens [lo, hi) into this rank's
+// receive buffer ([src][row - lo][H], local memory) and published its
+// completion epoch to flag[src]. Block b:
+//   1. waits until every rank's flag reached this call's epoch (bounded);
+//   2. sums the k partials of its share of [lo, hi) x H in fixed rank order
+//      (fp32) and stores the bf16 result into EVERY rank's output buffer
+//      (all-gather by push over NVLink);
+//   3. per-block barrier with its peers (phase 1 slots): after it, block b
+//      of every rank has pushed its share, so when the kernel has finished
+//      on this rank, the whole [T, H] output is present locally.
+__global__ void __launch_bounds__(kArThreads)
+    tp_rs_finish_kernel(ArPeers P, int rank, int k, int64_t in_off, int64_t out_off, int s_max,
+                        int T, int H, int64_t flag_off, uint32_t* __restrict__ gemm_epochs,
+                        uint32_t* __restrict__ epochs, int64_t timeout_ns, int* status) {
+  const uint32_t want = gemm_epochs[blockIdx.x] + 1;
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < k) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(P.base[rank] + flag_off) + threadIdx.x;
+    const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(timeout_ns);
+    while (static_cast<int32_t>(ld_acquire_sys(f) - want) < 0) {
+      if (globaltimer_ns() > deadline) {
+        set_status(status, kErrPeerTimeout, 210);
+        atomicExch(&ok, 0);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int lo = static_cast<int>(int64_t(T) * rank / k), hi = static_cast<int>(int64_t(T) * (rank + 1) / k);
+  const int hv = H / 8;  // 16-byte vectors per row
+  const int64_t nv = int64_t(hi - lo) * hv;
+  for (int64_t v = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; v < nv;
+       v += int64_t(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(v / hv), col = static_cast<int>(v % hv);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < k; ++r) {
+      const uint4* src = reinterpret_cast<const uint4*>(P.base[rank] + in_off) +
+                         (int64_t(r) * s_max + row) * hv + col;
+      uint4 x = __ldcg(src);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    for (int p = 0; p < k; ++p) {
+      const int q = (rank + p) % k;  // stagger destinations across ranks
+      uint4* dst = reinterpret_cast<uint4*>(P.base[q] + out_off) + (int64_t(lo) + row) * hv + col;
+      *dst = o;
+    }
+  }
+  const uint32_t epoch = epochs[blockIdx.x] + 1;
+  if (!block_barrier(P, rank, k, 1, epoch, timeout_ns, status)) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    epochs[blockIdx.x] = epoch;
+    gemm_epochs[blockIdx.x] = want;
+  }
+}
+
+void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
+                  int64_t s_max, int64_t T, int64_t H, int64_t flag_off, torch::Tensor gemm_epochs,
+                  torch::Tensor epochs, double timeout_s) {
+  const int k = static_cast<int>(bases.size());
+  TORCH_CHECK(k >= 2 && k <= kArMaxRanks);
+  TORCH_CHECK(H % 8 == 0 && in_off % 16 == 0 && out_off % 16 == 0 && flag_off % 4 == 0);
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= kArBlocks);
+  TORCH_CHECK(gemm_epochs.scalar_type() == at::kInt && gemm_epochs.numel() >= kArBlocks);
+  ArPeers P;
+  for (int r = 0; r < kArMaxRanks; ++r) P.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
+  tp_rs_finish_kernel<<<kArBlocks, kArThreads, 0, cur_stream()>>>(
+      P, static_cast<int>(rank), k, in_off, out_off, static_cast<int>(s_max), static_cast<int>(T),
+      static_cast<int>(H), flag_off, reinterpret_cast<uint32_t*>(gemm_epochs.data_ptr<int32_t>()),
+      reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>()),
+      static_cast<int64_t>(timeout_s * 1e9), status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+}
+
 // Test hook: one bounded wait on a flag nobody sets (single GPU, no peer):
 // must return with kErrPeerTimeout recorded, the context still usable.
 __global__ void flag_wait_probe_kernel(const uint32_t* flag, uint32_t want, int64_t timeout_ns,

@@ -67,6 +67,14 @@ class TPGroup:
         """Concatenate vocab-parallel logits along the last dim."""
         return x
 
+    def linear_reduce(self, x: torch.Tensor, w: torch.Tensor,
+                      b: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Row-parallel linear followed by the cross-rank sum (the bias, if
+        any, is added once)."""
+        if self.size > 1 and self.rank != 0:
+            b = None
+        return self.reduce(ops.linear(x, w, b))
+
 
 def _shard(n: int, rank: int, size: int):
     if n % size:
@@ -241,15 +249,18 @@ class DecoderModel:
             return ops.layer_norm(x, w, b, self.cfg.rms_norm_eps, residual)
         return ops.rms_norm(x, w, self.cfg.rms_norm_eps, residual)
 
-    def _attention(self, i: int, L, x: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor):
+    def _attention(self, i: int, L, x: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor,
+                   reduce: bool = True):
         c = self.cfg
         qkv = ops.linear(x, L.wqkv)
         q = ops.qkv_rope_cache(qkv, meta.positions, self.cos_sin, kv_cache, i, meta.slot_mapping,
                                self.local_heads, self.local_kv_heads, c.head_dim, c.rotary_dim,
                                L.bqkv)
         a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
-        return ops.linear(a.reshape(a.shape[0], -1), L.wo,
-                          out=self._reduce_slot(a.shape[0]))
+        a2 = a.reshape(a.shape[0], -1)
+        if reduce:  # o_proj + cross-rank sum (one fused GEMM -> reduce-scatter under TP)
+            return self.tp.linear_reduce(a2, L.wo)
+        return ops.linear(a2, L.wo)
 
     def _reduce_slot(self, T: int):
         """Where a row-parallel GEMM should write its partial output: the
@@ -259,18 +270,21 @@ class DecoderModel:
             return self.tp.reduce_buffer(T, self.cfg.hidden_size)
         return None
 
-    def _mlp(self, L, x: torch.Tensor) -> torch.Tensor:
+    def _mlp(self, L, x: torch.Tensor, reduce: bool = True) -> torch.Tensor:
         c = self.cfg
         if c.num_experts:
             from ..parallel.moe import moe_forward
-            return moe_forward(self, L, x)
+            y = moe_forward(self, L, x)
+            return self.tp.reduce(y) if reduce else y
         if c.hidden_act.startswith("gelu"):
             h = ops.linear(x, L.w1, L.b1)
             h = ops.gelu_tanh(h)
-            return ops.linear(h, L.w2)
+            return self.tp.linear_reduce(h, L.w2) if reduce else ops.linear(h, L.w2)
         h = ops.linear(x, L.w13)
         h = ops.silu_and_mul(h)
-        return ops.linear(h, L.w2, out=self._reduce_slot(h.shape[0]))
+        if reduce:  # down_proj + cross-rank sum
+            return self.tp.linear_reduce(h, L.w2)
+        return ops.linear(h, L.w2)
 
     def forward(self, input_ids: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor) -> torch.Tensor:
         """Returns final hidden states of the rows in ``meta.logits_idx``."""
@@ -280,8 +294,8 @@ class DecoderModel:
         for i, L in enumerate(self.layers):
             if c.parallel_block:
                 x, _ = self._norm(h, L.ln1, L.ln1_b)
-                a = self._attention(i, L, x, meta, kv_cache)
-                m = self._mlp(L, x)
+                a = self._attention(i, L, x, meta, kv_cache, reduce=False)
+                m = self._mlp(L, x, reduce=False)
                 s = a + m
                 if self.tp.rank == 0:  # row-parallel biases are added once
                     if L.bo is not None:
@@ -292,9 +306,9 @@ class DecoderModel:
                 h = h + s
                 continue
             x, residual = self._norm(h, L.ln1, L.ln1_b, residual)
-            a = self.tp.reduce(self._attention(i, L, x, meta, kv_cache))
+            a = self._attention(i, L, x, meta, kv_cache)
             x, residual = self._norm(a, L.ln2, L.ln2_b, residual)
-            h = self.tp.reduce(self._mlp(L, x))
+            h = self._mlp(L, x)
         if c.parallel_block:
             last = h.index_select(0, meta.logits_idx)
             x, _ = self._norm(last, self.norm_w, self.norm_b)

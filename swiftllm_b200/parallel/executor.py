@@ -239,8 +239,8 @@ class LocalExecutor:
                                       f"(code {p.exitcode})")
         for r in range(1, self.world):
             age = self.channel.heartbeat_age(r)
-            # age > 1e6 s: the worker has not attached yet (still loading)
-            if PEER_TIMEOUT < age < 1e6:
+            # age < 0: the worker has not attached yet (still loading)
+            if age > PEER_TIMEOUT:
                 raise WorkerDiedError(f"tensor-parallel rank {r} heartbeat lost "
                                       f"({age:.1f} s old)")
 

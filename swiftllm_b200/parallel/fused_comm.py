@@ -8,8 +8,20 @@ partials with peer loads and per-block release/acquire flags, so no NCCL
 call sits on the per-layer path. The vocab-parallel logits gather stays on
 NCCL (one small call per step).
 
+Fused GEMM -> all-reduce (``linear_reduce`` for o_proj and down_proj, on
+when SWIFTLLM_FUSED_GEMM_RS=1): the GEMM epilogue stores each output row
+straight into the receive buffer of the rank that owns that token
+(reduce-scatter by NVLink stores, overlapped with the remaining GEMM tiles)
+and publishes a completion epoch; ``tp_rs_finish`` then sums each rank's own
+tokens and pushes them to every rank (all-gather by stores). Otherwise the
+GEMM writes this rank's partial into its symmetric slot and ``reduce`` runs
+the two-shot reduction kernel.
+
 Layout of the symmetric allocation (bytes):
-  [flags 64 KiB | in A | in B | red A | red B], each buffer max_tokens x H bf16.
+  [flags 64 KiB | in A | in B | red A | red B], each buffer (max_tokens + 8) x H
+  bf16. Flags: [phase][block][rank] u32 barrier slots at 0, the fused GEMM's
+  per-source completion epochs at 8 KiB. `in` doubles as the fused receive
+  buffer [src rank][ceil(max_tokens / k)][H].
 """
 
 from __future__ import annotations
@@ -26,6 +38,8 @@ from .failures import CommTimeoutError
 log = get_logger(__name__)
 
 _FLAGS_BYTES = 64 << 10
+_GEMM_FLAG_OFF = 8 << 10
+FUSED_GEMM = os.environ.get("SWIFTLLM_FUSED_GEMM_RS", "0") == "1"
 TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
 
 
@@ -39,8 +53,11 @@ class FusedTP(NcclTP):
         self.C = cuda_ext()
         self.device = device
         H = model_cfg.hidden_size
+        self.H = H
+        self.max_tokens = max_tokens
         self.max_elems = max_tokens * H
-        self.buf_bytes = (self.max_elems * 2 + 255) // 256 * 256
+        self.s_max = (max_tokens + size - 1) // size
+        self.buf_bytes = ((max_tokens + 8) * H * 2 + 255) // 256 * 256
         total = _FLAGS_BYTES + 4 * self.buf_bytes
         self.symm = symm_mem.empty(total // 2, dtype=torch.bfloat16, device=device)
         self.symm.zero_()
@@ -49,6 +66,8 @@ class FusedTP(NcclTP):
         self.bases = [int(p) for p in self.hdl.buffer_ptrs]
         assert len(self.bases) == size
         self.epochs = torch.zeros(64, dtype=torch.int32, device=device)
+        self.gemm_ctr = torch.zeros(4, dtype=torch.int32, device=device)
+        self.gemm_epochs = torch.zeros(64, dtype=torch.int32, device=device)
         self.call = 0
         dist.barrier()
         log.info("fused TP comm ready: rank %d/%d, %.1f MiB symmetric", rank, size,
@@ -82,6 +101,29 @@ class FusedTP(NcclTP):
         ops._count()
         self.call += 1
         return out
+
+    def linear_reduce(self, x: torch.Tensor, w: torch.Tensor,
+                      b: Optional[torch.Tensor] = None, fused: Optional[bool] = None) -> torch.Tensor:
+        """Row-parallel linear + sum over ranks: either one fused GEMM ->
+        reduce-scatter kernel plus one reduce + all-gather kernel, or the GEMM
+        into this rank's slot plus the two-shot reduction."""
+        from .. import ops
+        T, H = x.shape[0], w.shape[0]
+        if self.rank != 0:
+            b = None
+        fused = FUSED_GEMM if fused is None else fused
+        if (not fused or T == 0 or T > self.max_tokens or H != self.H
+                or ops.gemm_backend() != "tcgen05"):
+            return self.reduce(ops.linear(x, w, b, out=self.reduce_buffer(T, H)))
+        parity = self.call % 2
+        in_off, red_off = self._off("in", parity), self._off("red", parity)
+        n = self.C.gemm_rs(x, w, b, self.bases, self.rank, in_off, self.s_max, _GEMM_FLAG_OFF,
+                           self.gemm_ctr)
+        self.C.tp_rs_finish(self.bases, self.rank, in_off, red_off, self.s_max, T, H,
+                            _GEMM_FLAG_OFF, self.gemm_epochs, self.epochs, TIMEOUT_S)
+        ops._count(n + 1)
+        self.call += 1
+        return self.symm[red_off // 2:red_off // 2 + T * H].view(T, H)
 
     def check(self) -> None:
         st = self.C.read_status(True)

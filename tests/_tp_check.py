@@ -52,6 +52,21 @@ def main():
             ref = torch.stack([p.float() for p in parts]).sum(0)
             got = tp.reduce(x.clone())
             torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=3e-2)
+        # fused GEMM -> reduce-scatter -> all-gather: sum over ranks of x_r . w_r^T
+        H = cfg.hidden_size
+        for T in (1, 7, 100, 256, 300, 7):
+            x = torch.randn(T, 64, device=dev, generator=g).to(dtype)
+            w = (torch.randn(H, 64, device=dev, generator=g) * 0.1).to(dtype)
+            xs = [torch.empty_like(x) for _ in range(world)]
+            ws = [torch.empty_like(w) for _ in range(world)]
+            dist.all_gather(xs, x)
+            dist.all_gather(ws, w)
+            ref = sum(a.float() @ b.float().t() for a, b in zip(xs, ws))
+            for fused in (True, False):
+                got = tp.linear_reduce(x, w, fused=fused)
+                torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=3e-2)
+        st = tp.C.read_status(True)
+        assert st[0] == 0, st
     m = DecoderModel(cfg, dtype, dev, tp)
     m.allocate()
     m.init_dummy(0)
