@@ -8,8 +8,8 @@ partials with peer loads and per-block release/acquire flags, so no NCCL
 call sits on the per-layer path. The vocab-parallel logits gather stays on
 NCCL (one small call per step).
 
-Fused GEMM -> all-reduce (``linear_reduce`` for o_proj and down_proj, on
-when SWIFTLLM_FUSED_GEMM_RS=1): the GEMM epilogue stores each output row
+Fused GEMM -> all-reduce (``linear_reduce`` for o_proj and down_proj, the
+default; SWIFTLLM_FUSED_GEMM_RS=0 turns it off): the GEMM epilogue stores each output row
 straight into the receive buffer of the rank that owns that token
 (reduce-scatter by NVLink stores, overlapped with the remaining GEMM tiles)
 and publishes a completion epoch; ``tp_rs_finish`` then sums each rank's own
@@ -39,7 +39,7 @@ log = get_logger(__name__)
 
 _FLAGS_BYTES = 64 << 10
 _GEMM_FLAG_OFF = 8 << 10
-FUSED_GEMM = os.environ.get("SWIFTLLM_FUSED_GEMM_RS", "0") == "1"
+FUSED_GEMM = os.environ.get("SWIFTLLM_FUSED_GEMM_RS", "1") == "1"
 TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
 
 
