@@ -66,6 +66,9 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("-p", "--port", type=int, default=8000)
     s.add_argument("--api-key", default=None)
     s.add_argument("--served-model-name", default=None)
+    s.add_argument("--frontend", choices=["native", "fastapi"], default="native",
+                   help="native: C++ HTTP/SSE front end driving the engine directly; "
+                        "fastapi: ASGI app over AsyncLLM")
     g = sub.add_parser("generate", help="Run offline generation")
     _engine_args(g)
     g.add_argument("-p", "--prompt", action="append", default=None)
@@ -111,11 +114,16 @@ def build_parser() -> argparse.ArgumentParser:
 
 def cmd_serve(a) -> int:
     from .config import ServerConfig
+    cfg = ServerConfig(host=a.host, port=a.port, api_key=a.api_key,
+                       served_model_name=a.served_model_name)
+    if getattr(a, "frontend", "native") == "native":
+        from .engine.llm import LLM
+        from .server.native_server import serve_native
+        serve_native(LLM(a.model, **_engine_kwargs(a)), cfg)
+        return 0
     from .engine.llm import AsyncLLM
     from .server.openai_server import serve
-    llm = AsyncLLM(a.model, **_engine_kwargs(a))
-    serve(llm, ServerConfig(host=a.host, port=a.port, api_key=a.api_key,
-                            served_model_name=a.served_model_name))
+    serve(AsyncLLM(a.model, **_engine_kwargs(a)), cfg)
     return 0
 
 

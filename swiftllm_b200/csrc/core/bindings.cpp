@@ -14,6 +14,7 @@
 #include "sampler.h"
 #include "scheduler.h"
 #include "shm_channel.h"
+#include "http_server.h"
 
 namespace py = pybind11;
 using namespace swift;
@@ -441,4 +442,5 @@ PYBIND11_MODULE(_core, m) {
 
   bind_loaders(m);
   bind_shm_channel(m);
+  bind_http_server(m);
 }
