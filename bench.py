@@ -38,12 +38,34 @@ METRIC = "output tok/s at Llama-2-7B/70B TP1-8 (max over ranks); p50 TTFT & TPOT
 MODEL = "llama-2-7b"
 
 
-def workload(n_req: int, seed: int = 0):
+def workload(n_req: int, seed: int = 0, ins=(128, 1024), outs=(128, 512), vocab: int = 32000):
+    """Uniform-random token ids; input / output lengths uniform in the closed
+    ranges (a fixed length when lo == hi)."""
     rng = np.random.default_rng(seed)
-    ins = rng.integers(128, 1025, size=n_req)
-    outs = rng.integers(128, 513, size=n_req)
-    prompts = [rng.integers(0, 32000, size=int(i)).tolist() for i in ins]
-    return prompts, [int(o) for o in outs]
+    il = rng.integers(ins[0], ins[1] + 1, size=n_req)
+    ol = rng.integers(outs[0], outs[1] + 1, size=n_req)
+    prompts = [rng.integers(0, vocab, size=int(i)).tolist() for i in il]
+    return prompts, [int(o) for o in ol]
+
+
+# Named workloads (the model/config shapes of the benchmark plan). "llama2-7b"
+# is the headline; the others exercise TP=8 on Llama-3-70B and MoE on Mixtral.
+WORKLOADS = {
+    "llama2-7b": dict(model="llama-2-7b", requests=1000, ins=(128, 1024), outs=(128, 512),
+                      max_num_seqs=256, max_model_len=2048, vocab=32000,
+                      desc="Llama-2-7B architecture (32L, H4096, 32 heads MHA, FFN 11008, V32000)"),
+    "llama3-70b-decode": dict(model="llama-3-70b", requests=256, ins=(2048, 2048), outs=(256, 256),
+                              max_num_seqs=256, max_model_len=2304, vocab=128256,
+                              desc="Llama-3-70B architecture (80L, H8192, 64/8 heads, FFN 28672, "
+                                   "V128256), decode-heavy: 256 x (2048 in, 256 out)"),
+    "llama3-70b-prefill": dict(model="llama-3-70b", requests=64, ins=(4096, 4096), outs=(16, 16),
+                               max_num_seqs=64, max_model_len=4112, vocab=128256,
+                               desc="Llama-3-70B architecture, prefill-heavy: 64 x (4096 in, 16 out)"),
+    "mixtral": dict(model="mixtral-8x7b", requests=512, ins=(256, 1024), outs=(256, 256),
+                    max_num_seqs=256, max_model_len=1280, vocab=32000,
+                    desc="Mixtral-8x7B architecture (32L, H4096, 32/8 heads, 8 experts top-2, "
+                         "FFN 14336), experts split over the TP ranks"),
+}
 
 
 class ClockSampler:
@@ -197,14 +219,19 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--requests", type=int, default=1000)
-    ap.add_argument("--model", default=MODEL)
-    ap.add_argument("--max-num-seqs", type=int, default=256)
+    ap.add_argument("--requests", type=int, default=None)
+    ap.add_argument("--model", default=None)
+    ap.add_argument("--workload", default="llama2-7b", choices=sorted(WORKLOADS))
+    ap.add_argument("--max-num-seqs", type=int, default=None)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
     ap.add_argument("--profile-host", action="store_true",
                     help="report host phases and the GPU idle gap between steps (diagnostic)")
     args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    args.model = args.model or wl["model"]
+    args.requests = args.requests or wl["requests"]
+    args.max_num_seqs = args.max_num_seqs or wl["max_num_seqs"]
     if args.impl == "reference":
         reference_arm(args)
         return
@@ -221,14 +248,14 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
     ekw = dict(load_format="dummy", dtype="bfloat16", tensor_parallel_size=args.gpus,
                gpu_memory_utilization=0.9, block_size=16, max_num_seqs=args.max_num_seqs,
-               enable_chunked_prefill=True, max_num_batched_tokens=8192, max_model_len=2048,
+               enable_chunked_prefill=True, max_num_batched_tokens=8192, max_model_len=wl["max_model_len"],
                comm_backend=args.comm, seed=0, preemption_mode="recompute")
     if rank != 0:
         from swiftllm_b200.parallel.executor import run_worker_from_env
         run_worker_from_env(EngineConfig(model=args.model, **ekw))
         return
 
-    prompts, out_lens = workload(args.requests)
+    prompts, out_lens = workload(args.requests, 0, wl["ins"], wl["outs"], wl["vocab"])
     sps = [SamplingParams(temperature=0.0, max_tokens=o, ignore_eos=True) for o in out_lens]
     t_init = time.time()
     llm = LLM(args.model, **ekw)
@@ -293,9 +320,10 @@ def main() -> None:
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
         "config": {
-            "model": "Llama-2-7B architecture (32L, H4096, 32 heads MHA, FFN 11008, V32000)",
+            "model": wl["desc"],
+            "workload": args.workload,
             "global_batch": args.max_num_seqs,
-            "seq_len": "in U[128,1024], out U[128,512]",
+            "seq_len": f"in U[{wl['ins'][0]},{wl['ins'][1]}], out U[{wl['outs'][0]},{wl['outs'][1]}]",
             "requests": args.requests,
             "parallelism": f"tp{args.gpus}",
             "comm": args.comm if args.gpus > 1 else "none",
