@@ -33,6 +33,9 @@ void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
 torch::Tensor gemm_sk_stamps();
+void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x);
+int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                  torch::Tensor wscale, c10::optional<torch::Tensor> bias);
 int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
                 std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t s_max,
                 int64_t flag_off, torch::Tensor ctr);
@@ -74,6 +77,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_sk_stamps", &swift::gemm_sk_stamps);
   m.def("gemm_packed", &swift::gemm_packed);
   m.def("gemm_rs", &swift::gemm_rs);
+  m.def("gemm_e4m3", &swift::gemm_e4m3);
+  m.def("quantize_e4m3", &swift::quantize_e4m3);
   m.def("tp_rs_finish", &swift::tp_rs_finish);
   m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);

@@ -32,6 +32,8 @@
 #include <algorithm>
 #include <cstdlib>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace swift {
@@ -85,6 +87,19 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// kind::f8f6f4 with A and B both E4M3 (format code 0), fp32 accumulate.
+template <int BN>
+__host__ __device__ constexpr uint32_t instr_desc_e4m3() {
+  return (1u << 4) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>(kGemmBM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -206,13 +221,19 @@ struct GemmSmem {
   static constexpr size_t BYTES = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP8 = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
                         int64_t ldy, const __nv_bfloat16* __restrict__ bias,
                         float* __restrict__ ws, int M, int N, int K, int splits, int* status,
-                        const int32_t* __restrict__ goff, int groups, const ScatterDesc sc) {
+                        const int32_t* __restrict__ goff, int groups, const ScatterDesc sc,
+                        const float* __restrict__ wscale = nullptr,
+                        const float* __restrict__ xscale = nullptr) {
+  // FP8 (E4M3 weights and activations, per-row scales): a 128-byte smem row
+  // holds 128 elements, so one stage covers 128 of K; scales are applied in
+  // the epilogue.
+  constexpr int kBK = FP8 ? 128 : kGemmBK;
   using S = GemmSmem<BN, STAGES>;
   // Grouped mode (goff != nullptr, MoE experts): group g multiplies the token
   // rows [goff[g], goff[g+1]) by weight rows [g*M, (g+1)*M); tiles never
@@ -232,7 +253,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + kGemmBM - 1) / kGemmBM;
   const int n_tiles = (N + BN - 1) / BN;
-  const int k_iters = (K + kGemmBK - 1) / kGemmBK;
+  const int k_iters = (K + kBK - 1) / kBK;
   const int k_per = (k_iters + splits - 1) / splits;
   int total = m_tiles * n_tiles * splits;
   if (goff) {
@@ -314,8 +335,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
-          tma_load_2d(a, &tm_w, kk * kGemmBK, w0, &full[st]);
-          tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, x0, &full[st]);
+          tma_load_2d(a, &tm_w, kk * kBK, w0, &full[st]);
+          tma_load_2d(a + S::A_BYTES, &tm_x, kk * kBK, x0, &full[st]);
         }
       }
       if (!ok) {  // let the loads already issued land before the CTA exits
@@ -326,7 +347,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = instr_desc_bf16<BN>();
+      constexpr uint32_t idesc = FP8 ? instr_desc_e4m3<BN>() : instr_desc_bf16<BN>();
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tc) {
@@ -352,7 +373,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
 #pragma unroll
           for (int j = 0; j < kGemmBK / 16; ++j)  // +32 B along K inside the swizzle atom
-            umma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+            if constexpr (FP8)
+              umma_e4m3(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+            else
+              umma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
           umma_commit(&empty[st]);
         }
         if (!ok) break;
@@ -388,6 +412,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int f = m * kGemmBM + q * 32 + lane;
       const float b = (bias != nullptr && f < M && splits == 1) ? __bfloat162float(bias[f]) : 0.f;
+      const float wsf = (FP8 && f < M) ? wscale[f] : 1.f;
+      auto dq = [&](float a, int t) { return FP8 ? a * wsf * xscale[min(t, N - 1)] : a; };
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       if constexpr (BN >= 32) {
 #pragma unroll 1
@@ -402,11 +428,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (t0 + j < xend)
-                  (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(v[j] + b);
+                  (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(dq(v[j], t0 + j) + b);
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (t0 + j < N) ws[(int64_t(s) * N + t0 + j) * M + f] = v[j];
+                if (t0 + j < N) ws[(int64_t(s) * N + t0 + j) * M + f] = dq(v[j], t0 + j);
             }
           }
         }
@@ -421,11 +447,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               if (t0 + j < xend)
-                (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(v[j] + b);
+                (run ? run + j * rs : sc_row(sc, y, ldy, t0 + j))[f] = __float2bfloat16(dq(v[j], t0 + j) + b);
           } else {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
-              if (t0 + j < N) ws[(int64_t(s) * N + t0 + j) * M + f] = v[j];
+              if (t0 + j < N) ws[(int64_t(s) * N + t0 + j) * M + f] = dq(v[j], t0 + j);
           }
         }
       }
@@ -866,13 +892,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // 2-D bf16 tensor [rows, cols] with row stride `ld` elements; box 64 x box_rows.
-static CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// fp8 = true: 1-byte elements, 128 per 128-byte box row.
+static CUtensorMap make_tmap(const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                             bool fp8 = false) {
   CUtensorMap tm;
+  const int es = fp8 ? 1 : 2;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(kGemmBK), static_cast<cuuint32_t>(box_rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / es), static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = get_encode()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+  CUresult r = get_encode()(&tm, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                            2, const_cast<void*>(ptr), dims,
                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -888,13 +918,14 @@ static int num_sms() {
   return n[dev];
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool FP8 = false>
 static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloat16* y, int64_t ldy,
                         const __nv_bfloat16* bias, float* ws, int M, int N, int K, int splits,
                         const int32_t* goff = nullptr, int groups = 0,
-                        const ScatterDesc& sc = ScatterDesc{}) {
+                        const ScatterDesc& sc = ScatterDesc{}, const float* wscale = nullptr,
+                        const float* xscale = nullptr) {
   using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tcgen05_kernel<BN, STAGES>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, FP8>;
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -907,7 +938,8 @@ static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloa
   const int tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN + (goff ? groups : 0)) * splits;
   const int grid = std::min(tiles, num_sms());
   kern<<<grid, kGemmThreads, S::BYTES, cur_stream()>>>(tw, tx, y, ldy, bias, ws, M, N, K, splits,
-                                                       status_word_ptr(), goff, groups, sc);
+                                                       status_word_ptr(), goff, groups, sc, wscale,
+                                                       xscale);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -1178,6 +1210,96 @@ int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_
   TORCH_CHECK(gemm_streamk(reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), x, wp,
                            bp, T, ldx, ldy, static_cast<int>(M), static_cast<int>(wp.size(1))),
               "gemm_packed: no stream-K plan");
+  return 1;
+}
+
+// ---- FP8 (E4M3) weights and activations
+// Per-row symmetric quantisation: scale = max|row| / 448 (the largest finite
+// E4M3 value), q = round-to-nearest E4M3 of x / scale, saturating. Used for
+// weights at load time (one scale per output feature) and for activations
+// before every FP8 GEMM (one scale per token).
+__global__ void quantize_e4m3_kernel(uint8_t* __restrict__ q, float* __restrict__ scale,
+                                     const __nv_bfloat16* __restrict__ x, int K, int64_t ldx) {
+  const int64_t r = blockIdx.x;
+  const __nv_bfloat16* row = x + r * ldx;
+  float m = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(__bfloat162float(row[k])));
+  __shared__ float red[32];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float s = fmaxf(red[0] / 448.f, 1e-12f);
+  const float inv = 1.f / s;
+  if (threadIdx.x == 0) scale[r] = s;
+  for (int k = threadIdx.x; k < K; k += blockDim.x)
+    q[r * K + k] = __nv_cvt_float_to_fp8(__bfloat162float(row[k]) * inv, __NV_SATFINITE, __NV_E4M3);
+}
+
+void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
+  CHECK_BF16(x);
+  TORCH_CHECK(q.scalar_type() == at::kByte && q.is_contiguous() && scale.scalar_type() == at::kFloat);
+  const int64_t K = x.size(-1), R = x.numel() / K;
+  TORCH_CHECK(x.stride(-1) == 1 && q.numel() == R * K && scale.numel() == R);
+  if (R == 0) return;
+  const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
+  quantize_e4m3_kernel<<<static_cast<unsigned>(R), 256, 0, cur_stream()>>>(
+      q.data_ptr<uint8_t>(), scale.data_ptr<float>(),
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), static_cast<int>(K), ldx);
+  SWIFT_CHECK_LAUNCH();
+}
+
+// out [T, M] bf16 = (xq * xscale) . (wq * wscale)^T (+ bias), on
+// tcgen05.mma kind::f8f6f4. xq [T, K], wq [M, K] uint8 holding E4M3 bits,
+// K a multiple of 16. Returns launches.
+int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                  torch::Tensor wscale, c10::optional<torch::Tensor> bias) {
+  CHECK_BF16(out);
+  TORCH_CHECK(xq.scalar_type() == at::kByte && wq.scalar_type() == at::kByte);
+  TORCH_CHECK(xq.is_contiguous() && wq.is_contiguous() && out.stride(-1) == 1);
+  TORCH_CHECK(xscale.scalar_type() == at::kFloat && wscale.scalar_type() == at::kFloat);
+  const int64_t K = xq.size(-1), T = xq.numel() / K, M = wq.size(0);
+  TORCH_CHECK(wq.size(1) == K && K % 16 == 0, "gemm_e4m3: K must match and be a multiple of 16");
+  TORCH_CHECK(xscale.numel() == T && wscale.numel() == M);
+  if (T == 0) return 0;
+  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M;
+  int bn, splits;
+  plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K / 2), &bn, &splits);
+  CUtensorMap tw = make_tmap(wq.data_ptr(), M, K, K, kGemmBM, true);
+  CUtensorMap tx = make_tmap(xq.data_ptr(), T, K, K, bn, true);
+  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+  const __nv_bfloat16* bp =
+      bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
+                       : nullptr;
+  torch::Tensor ws;
+  float* wsp = nullptr;
+  if (splits > 1) {
+    ws = torch::empty({splits, T, M}, out.options().dtype(torch::kFloat));
+    wsp = ws.data_ptr<float>();
+  }
+  const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K);
+  const float* wsc = wscale.data_ptr<float>();
+  const float* xsc = xscale.data_ptr<float>();
+  const ScatterDesc none{};
+  switch (bn) {
+    case 16: launch_gemm<16, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 32: launch_gemm<32, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 64: launch_gemm<64, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 128: launch_gemm<128, 6, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    default: launch_gemm<256, 4, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+  }
+  if (splits > 1) {
+    int64_t n = M * T;
+    int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 8));
+    splitk_reduce_kernel<<<blocks, 256, 0, cur_stream()>>>(y, ldy, wsp, bp, Mi, Ni, splits);
+    SWIFT_CHECK_LAUNCH();
+    return 2;
+  }
   return 1;
 }
 

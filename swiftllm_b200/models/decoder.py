@@ -173,7 +173,10 @@ class DecoderModel:
         yield "embed", self.embed
         for i, L in enumerate(self.layers):
             for k, v in vars(L).items():
-                if v is not None:
+                if isinstance(v, ops.Fp8Weight):
+                    yield f"layers.{i}.{k}.q", v.q
+                    yield f"layers.{i}.{k}.scale", v.scale
+                elif v is not None:
                     yield f"layers.{i}.{k}", v
         yield "norm", self.norm_w
         if self.norm_b is not None:
@@ -236,6 +239,18 @@ class DecoderModel:
         if leaf in ("lm_head", "lm_head_b") and self.vocab_end - self.vocab_start != c.vocab_size:
             return ("rows", c.vocab_size, [(0, self.vocab_start, self.vocab_end - self.vocab_start)])
         return None
+
+    def quantize_fp8(self) -> None:
+        """Replace the dense projection weights (QKV, o_proj, gate_up / fc1,
+        down / fc2) by E4M3 weights with per-output-feature scales. The
+        embedding, norms, LM head and MoE experts stay in the model dtype."""
+        for L in self.layers:
+            for name in ("wqkv", "wo", "w13", "w1", "w2"):
+                w = getattr(L, name, None)
+                if isinstance(w, torch.Tensor) and w.dim() == 2:
+                    setattr(L, name, ops.fp8_weight(w))
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
 
     def load_state(self, get: Callable[[str], Optional[torch.Tensor]]) -> None:
         """Fill weights from full (unsharded) HF-named tensors; ``get`` returns a

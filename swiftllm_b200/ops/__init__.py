@@ -90,8 +90,69 @@ def layer_norm(x, w, b, eps, residual=None):
     return out, residual
 
 
+class Fp8Weight:
+    """A linear weight stored as E4M3 (uint8 bits) with one fp32 scale per
+    output feature: w ~= q * scale[:, None]."""
+
+    def __init__(self, q: torch.Tensor, scale: torch.Tensor):
+        self.q = q
+        self.scale = scale
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequantize(self) -> torch.Tensor:
+        return self.q.view(torch.float8_e4m3fn).float() * self.scale[:, None]
+
+
+def quantize_e4m3(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-row E4M3 quantisation: (uint8 bits [R, K], fp32 scale [R]),
+    scale = max|row| / 448."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x2.is_cuda:
+        s = (x2.float().abs().amax(-1) / 448.0).clamp_min(1e-12)
+        q = (x2.float() / s[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+        return q, s
+    q = torch.empty(x2.shape, dtype=torch.uint8, device=x2.device)
+    s = torch.empty(x2.shape[0], dtype=torch.float32, device=x2.device)
+    cuda_ext().quantize_e4m3(q, s, x2)
+    _count()
+    return q, s
+
+
+def fp8_weight(w: torch.Tensor) -> Fp8Weight:
+    q, s = quantize_e4m3(w)
+    return Fp8Weight(q, s)
+
+
+def _linear_fp8(x, w: Fp8Weight, b, out):
+    if not x.is_cuda:
+        xq, xs = quantize_e4m3(x)
+        xd = xq.view(torch.float8_e4m3fn).float() * xs[:, None]
+        y = xd @ w.dequantize().t()
+        if b is not None:
+            y = y + b.float()
+        y = y.to(x.dtype).reshape(x.shape[:-1] + (w.shape[0],))
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    xq, xs = quantize_e4m3(x)
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)
+    _count(cuda_ext().gemm_e4m3(out, xq, xs, w.q, w.scale, b))
+    return out
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if isinstance(w, Fp8Weight):
+        return _linear_fp8(x, w, b, out)
     if not x.is_cuda:
         return ref.linear(x, w, b)
     if _GEMM_BACKEND == "cublas":

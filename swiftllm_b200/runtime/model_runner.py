@@ -117,6 +117,11 @@ class ModelRunner:
             from ..loaders import open_checkpoint
             ckpt = open_checkpoint(model, fmt)
             self.model.load_state(ckpt.get)
+        q = getattr(self.ecfg.quantization, "value", self.ecfg.quantization)
+        if q == "fp8":
+            self.model.quantize_fp8()
+        elif q not in (None, "none"):
+            raise NotImplementedError(f"quantization {q!r} is not supported (fp8 is)")
         if self.is_cuda:
             torch.cuda.synchronize(self.device)
         log.info("weights ready in %.1fs (%s, rank %d/%d)", time.time() - t0, fmt,

@@ -333,6 +333,24 @@ def mixed_sweep():
     return res
 
 
+def fp8_case(T, N, K):
+    """E4M3 GEMM (per-row scales) vs the bf16 GEMM of the same shape; the fp8
+    time includes the activation quantisation kernel."""
+    from .. import ops
+    C = cuda_ext()
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    fw = ops.fp8_weight(w)
+    y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+    t8 = _time(lambda: ops.linear(x, fw, out=y))
+    t16 = _time(lambda: C.gemm(y, x, w, None))
+    pk = measured_peaks()
+    byts = N * K + T * K * 3 + T * N * 2
+    return {"op": "gemm_e4m3", "T": T, "N": N, "K": K, "fp8_ms": round(t8, 4), "bf16_ms": round(t16, 4),
+            "fp8_TB/s": round(byts / t8 / 1e9, 2), "fp8_TFLOP/s": round(2.0 * T * N * K / t8 / 1e9, 1),
+            "frac_bw": round(byts / t8 / 1e9 / (pk["hbm_gbs"] / 1e3), 3)}
+
+
 def sweep():
     res = []
     for T, N, K in [(256, 12288, 4096), (256, 4096, 4096), (256, 22016, 4096), (256, 4096, 11008),
@@ -351,7 +369,7 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest", "mixed"])
+    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest", "mixed", "fp8"])
     ap.add_argument("--model", default="llama-2-7b")
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
@@ -364,6 +382,12 @@ def main(argv=None):
     elif a.op == "skstamps":
         shp = [int(v) for v in (a.shape or "256,12288,4096,1,16").split(",")]
         res = sk_stamps(*shp)
+    elif a.op == "fp8":
+        res = [fp8_case(*[int(v) for v in c.split("x")]) for c in
+               (a.shape or "256x12288x4096,256x22016x4096,256x4096x11008,8192x12288x4096").split(",")]
+        for r in res:
+            print(json.dumps(r), flush=True)
+        res = None
     elif a.op == "mixed":
         res = mixed_sweep()
     elif a.op == "packtest":

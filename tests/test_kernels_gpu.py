@@ -317,3 +317,37 @@ def test_moe_route_permute_grouped_gemm_combine(C):
             ref.index_add_(0, rows, (hh @ w2[le].float().cpu().t()) * w.cpu()[rows, slot].unsqueeze(1))
         torch.testing.assert_close(out.float().cpu(), ref, rtol=3e-2, atol=3e-2)
     _status_ok(C)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (37, 640, 256), (256, 12288, 4096),
+                                   (700, 4096, 11008)])
+def test_gemm_e4m3(C, T, N, K):
+    from swiftllm_b200 import ops
+    x = bf(T, K, scale=0.5)
+    w = bf(N, K, scale=0.05)
+    xq, xs = ops.quantize_e4m3(x)
+    wq, wsc = ops.quantize_e4m3(w)
+    # quantiser matches torch's E4M3 conversion of the same scaled values
+    xs_ref = (x.float().abs().amax(-1) / 448).clamp_min(1e-12)
+    torch.testing.assert_close(xs, xs_ref, rtol=1e-6, atol=0)
+    q_ref = (x.float() / xs_ref[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8)
+    # x * (1/s) vs x / s can round differently right at a rounding boundary
+    assert (xq != q_ref).float().mean().item() < 1e-2
+    out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+    C.gemm_e4m3(out, xq, xs, wq, wsc, None)
+    xd = xq.view(torch.float8_e4m3fn).float() * xs[:, None]
+    wd = wq.view(torch.float8_e4m3fn).float() * wsc[:, None]
+    r = xd @ wd.t()
+    torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=2e-2 * math.sqrt(K / 64) * 0.5)
+    _status_ok(C)
+
+
+def test_fp8_model_gpu():
+    from swiftllm_b200 import LLM, SamplingParams
+    sp = SamplingParams(temperature=0, max_tokens=16, ignore_eos=True)
+    prompts = [[5, 6, 7, 8, 9, 10, 11, 12] * 4, list(range(100, 164))]
+    llm = LLM("tiny-llama", load_format="dummy", dtype="bfloat16", gpu_memory_utilization=0.3,
+              max_model_len=256, quantization="fp8")
+    out = llm.generate(prompt_token_ids=prompts, sampling_params=sp, use_tqdm=False)
+    assert all(len(o.outputs[0].token_ids) == 16 for o in out)
+    llm.shutdown()
