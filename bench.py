@@ -253,7 +253,7 @@ def main() -> None:
     if rank != 0:
         from swiftllm_b200.parallel.executor import run_worker_from_env
         run_worker_from_env(EngineConfig(model=args.model, **ekw))
-        return
+        _exit_now()
 
     prompts, out_lens = workload(args.requests, 0, wl["ins"], wl["outs"], wl["vocab"])
     sps = [SamplingParams(temperature=0.0, max_tokens=o, ignore_eos=True) for o in out_lens]
@@ -347,6 +347,16 @@ def main() -> None:
         res["host_profile"] = prof.report()
     print(json.dumps(res), flush=True)
     llm.shutdown()
+    _exit_now()
+
+
+def _exit_now() -> None:
+    """Leave without running library teardown: the result is printed and
+    flushed, the workers are shut down, and NCCL / symmetric-memory
+    destructors at interpreter exit have aborted some multi-rank runs."""
+    sys.stdout.flush()
+    sys.stderr.flush()
+    os._exit(0)
 
 
 if __name__ == "__main__":
