@@ -1049,7 +1049,9 @@ static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per,
   const int units = (M + 128 * m - 1) / (128 * m) * ((N + b - 1) / b);
   if (units > kSkMaxTiles) return false;
   const int64_t total = int64_t(units) * k_iters;
-  const int min_per = std::max(1, env_int("SWIFT_SK_MINPER", 32));
+  // at least 32 k-iterations per CTA, but never more than one tile's worth
+  // (short K: one CTA per tile keeps every tile's CTA busy)
+  const int min_per = std::max(1, std::min(env_int("SWIFT_SK_MINPER", 32), k_iters));
   int g = static_cast<int>(std::min<int64_t>(sms, (total + min_per - 1) / min_per));
   g = std::max(g, 1);
   int p = static_cast<int>((total + g - 1) / g);
