@@ -43,6 +43,7 @@ class _Req:
     logprobs: Dict[int, List[TokenLogprob]] = field(default_factory=dict)
     finished_seqs: Dict[int, str] = field(default_factory=dict)
     done: bool = False
+    arrival: float = 0.0
 
 
 def prepare_config(c: EngineConfig):
@@ -88,6 +89,7 @@ class LLMEngine:
         self.io_bytes = [0, 0]
         self.num_steps = 0
         self.step_hook = None
+        self._fatal: Optional[BaseException] = None  # a dead worker / peer: the engine is unusable
 
     # ------------------------------------------------------------ init
     def _ensure_initialized(self) -> None:
@@ -141,6 +143,8 @@ class LLMEngine:
                     arrival_time: Optional[float] = None, priority: int = 0,
                     stream: bool = False) -> None:
         self._ensure_initialized()
+        if self._fatal is not None:
+            raise self._fatal
         if request_id in self._reqs:
             raise ValueError(f"duplicate request id {request_id!r}")
         sp = sampling_params or SamplingParams()
@@ -171,7 +175,8 @@ class LLMEngine:
         if ids.size and (ids.min() < 0 or ids.max() >= self.model_config.vocab_size):
             raise ValueError("prompt token id out of vocabulary range")
         gid = self.scheduler.add_request(request_id, ids, gp, arrival)
-        r = _Req(request_id, prompt, list(map(int, prompt_token_ids)), sp, gid, stream=stream)
+        r = _Req(request_id, prompt, list(map(int, prompt_token_ids)), sp, gid, stream=stream,
+                 arrival=arrival)
         self._reqs[request_id] = r
         self._by_gid[gid] = r
         self._prompt_tokens += len(prompt_token_ids)
@@ -199,8 +204,41 @@ class LLMEngine:
         return prompt[:n], prompt[n:]
 
     def step(self) -> List[RequestOutput]:
+        """One engine iteration. If a tensor-parallel worker dies or a peer
+        stops answering, every in-flight request is finished with
+        finish_reason "abort" in this call's outputs and the engine raises
+        that error on any later use."""
         self._ensure_initialized()
+        if self._fatal is not None:
+            raise self._fatal
+        from ..parallel.failures import CommTimeoutError, WorkerDiedError
+        try:
+            return self._step()
+        except (WorkerDiedError, CommTimeoutError) as e:
+            log.error("engine stopped: %s; aborting %d in-flight requests", e,
+                      self.get_num_unfinished_requests())
+            self._fatal = e
+            outs = []
+            for r in list(self._reqs.values()):
+                if not r.done:
+                    self.scheduler.abort_request(r.request_id)
+                    outs.append(self._final_output(r, aborted=True))
+            return outs
+
+    def _expire(self) -> None:
+        """Abort requests older than request_timeout_secs (0 disables)."""
+        limit = float(getattr(self.config, "request_timeout_secs", 0) or 0)
+        if limit <= 0:
+            return
+        now = time.monotonic()
+        for r in self._reqs.values():
+            if not r.done and r.request_id not in self._aborted and now - r.arrival > limit:
+                log.warning("request %s timed out after %.0f s", r.request_id, now - r.arrival)
+                self.abort_request(r.request_id)
+
+    def _step(self) -> List[RequestOutput]:
         outs: List[RequestOutput] = []
+        self._expire()
         for rid in self._aborted:
             r = self._reqs.get(rid)
             if r is not None and not r.done:

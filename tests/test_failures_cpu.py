@@ -61,6 +61,26 @@ def test_dead_tp_worker_is_reported():
     pid = ex.procs[0].pid
     os.kill(pid, signal.SIGKILL)  # the worker this test spawned, by exact pid
     ex.procs[0].join(timeout=30)
+    # the step that finds the dead worker finishes the in-flight request as aborted
+    out = llm.generate(prompt_token_ids=[[5, 6, 7]], sampling_params=sp, use_tqdm=False)
+    assert out[0].outputs[0].finish_reason.value == "abort"
+    # and the engine refuses further work with the original error
     with pytest.raises(WorkerDiedError):
-        llm.generate(prompt_token_ids=[[5, 6, 7]], sampling_params=sp, use_tqdm=False)
+        llm.generate(prompt_token_ids=[[8, 9]], sampling_params=sp, use_tqdm=False)
     llm.shutdown()
+
+
+def test_request_timeout_aborts():
+    llm = LLM("tiny-llama", load_format="dummy", device="cpu", dtype="float32",
+              max_model_len=128, request_timeout_secs=0.05)
+    eng = llm.llm_engine
+    sp = SamplingParams(temperature=0, max_tokens=100, ignore_eos=True)
+    eng.add_request("slow", prompt_token_ids=[1, 2, 3], sampling_params=sp)
+    outs = []
+    t0 = time.time()
+    while eng.has_unfinished_requests() and time.time() - t0 < 60:
+        outs += eng.step()
+        time.sleep(0.01)
+    fin = [o for o in outs if o.finished]
+    assert fin and fin[0].outputs[0].finish_reason.value == "abort"
+    assert len(fin[0].outputs[0].token_ids) < 100
