@@ -157,6 +157,7 @@ struct ScatterDesc {
   int64_t flag_off;   // byte offset of the [src rank] u32 completion flags
   uint32_t* ctr;      // this rank's device counters: [0] epoch, [2] CTA done count
   int k, rank, s_max, T, H;
+  int fence_all;      // 1: every thread fences its own stores before the CTA publishes
 };
 
 __device__ __forceinline__ int sc_owner(const ScatterDesc& sc, int t) {
@@ -192,7 +193,7 @@ __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
 // the last CTA to finish bumps the epoch and publishes it to every rank.
 __device__ __forceinline__ void sc_publish(const ScatterDesc& sc) {
   if (sc.k == 0) return;
-  __threadfence_system();
+  if (sc.fence_all) __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();
@@ -1187,6 +1188,10 @@ int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b
   sc.s_max = static_cast<int>(s_max);
   sc.T = static_cast<int>(T);
   sc.H = static_cast<int>(H);
+  // every thread fences its remote stores before the CTA publishes
+  // (SWIFT_RS_FENCE_ALL=0: only thread 0 after bar.sync, the split-K
+  // semaphore pattern, which relies on the fence's cumulativity)
+  sc.fence_all = env_int("SWIFT_RS_FENCE_ALL", 1);
   if (T == 0) return 0;
   return gemm_impl(nullptr, 0, x, w, bias, sc);
 }
