@@ -164,6 +164,13 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     C = cuda_ext()
     if out is None:
         out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)
+    K = x.shape[-1]
+    if K % 8:
+        # TMA rows must be 16-byte multiples: zero-pad K (odd shard widths,
+        # e.g. a small FFN split over many ranks)
+        pad = 8 - K % 8
+        x = torch.nn.functional.pad(x, (0, pad))
+        w = torch.nn.functional.pad(w, (0, pad))
     _count(C.gemm(out, x, w, b))
     return out
 

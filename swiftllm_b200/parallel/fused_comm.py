@@ -112,7 +112,8 @@ class FusedTP(NcclTP):
         if self.rank != 0:
             b = None
         fused = FUSED_GEMM if fused is None else fused
-        if (not fused or not isinstance(w, torch.Tensor) or T == 0 or T > self.max_tokens or H != self.H
+        if (not fused or not isinstance(w, torch.Tensor) or x.shape[-1] % 8 or T == 0
+                or T > self.max_tokens or H != self.H
                 or ops.gemm_backend() != "tcgen05"):
             return self.reduce(ops.linear(x, w, b, out=self.reduce_buffer(T, H)))
         parity = self.call % 2

@@ -351,3 +351,11 @@ def test_fp8_model_gpu():
     out = llm.generate(prompt_token_ids=prompts, sampling_params=sp, use_tqdm=False)
     assert all(len(o.outputs[0].token_ids) == 16 for o in out)
     llm.shutdown()
+
+
+def test_linear_odd_k():
+    # K not a multiple of 8 (16-byte TMA rows): ops.linear zero-pads
+    from swiftllm_b200 import ops
+    x, w = bf(19, 172, scale=0.5), bf(96, 172, scale=0.05)
+    y = ops.linear(x, w)
+    torch.testing.assert_close(y.float(), x.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
