@@ -414,7 +414,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int f = m * kGemmBM + q * 32 + lane;
       const float b = (bias != nullptr && f < M && splits == 1) ? __bfloat162float(bias[f]) : 0.f;
       const float wsf = (FP8 && f < M) ? wscale[f] : 1.f;
-      auto dq = [&](float a, int t) { return FP8 ? a * wsf * xscale[min(t, N - 1)] : a; };
+      // FP8: scales applied once per chunk, before the stores (independent loads)
+      auto dq = [&](float a, int) { return a; };
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       if constexpr (BN >= 32) {
 #pragma unroll 1
@@ -422,6 +423,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int t0 = x0 + c * 32;
+          if constexpr (FP8) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] *= wsf * xscale[min(t0 + j, N - 1)];
+          }
           if (f < M) {
             if (splits == 1) {
               int64_t rs;
@@ -441,6 +446,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[16];
         tmem_ld16(tbase, v);
         const int t0 = x0;
+        if constexpr (FP8) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= wsf * xscale[min(t0 + j, N - 1)];
+        }
         if (f < M) {
           if (splits == 1) {
             int64_t rs;
