@@ -42,6 +42,10 @@ int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b
 void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
                   int64_t s_max, int64_t T, int64_t H, int64_t flag_off, torch::Tensor gemm_epochs,
                   torch::Tensor epochs, double timeout_s);
+void tp_rs_finish_norm(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
+                       int64_t res_off, torch::Tensor residual, torch::Tensor w, double eps,
+                       int64_t s_max, int64_t T, int64_t H, int64_t flag_off,
+                       torch::Tensor gemm_epochs, torch::Tensor epochs, double timeout_s);
 int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
                     c10::optional<torch::Tensor> bias);
 void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
@@ -80,6 +84,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_e4m3", &swift::gemm_e4m3);
   m.def("quantize_e4m3", &swift::quantize_e4m3);
   m.def("tp_rs_finish", &swift::tp_rs_finish);
+  m.def("tp_rs_finish_norm", &swift::tp_rs_finish_norm);
   m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
   m.def("gemm_grouped", &swift::gemm_grouped);

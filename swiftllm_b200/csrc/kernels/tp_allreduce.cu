@@ -241,6 +241,127 @@ void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int6
   SWIFT_CHECK_LAUNCH();
 }
 
+// tp_rs_finish with the following fused add + RMSNorm (the norm that opens
+// the next sub-block). Block b owns whole token rows of this rank's shard
+// (row lo + b, lo + b + gridDim, ...): it sums the k partials in rank order
+// (fp32, rounded to bf16 like the unfused reduce), adds the residual row
+// (rounded to bf16, the new residual), computes the RMS scale over the row,
+// and pushes both the new residual row and the normalised row to every
+// rank's `res_off` / `out_off` buffers. Same flags and barrier as
+// tp_rs_finish. H <= 4 * 8 * blockDim.x.
+__global__ void __launch_bounds__(kArThreads)
+    tp_rs_finish_norm_kernel(ArPeers P, int rank, int k, int64_t in_off, int64_t out_off,
+                             int64_t res_off, const __nv_bfloat16* __restrict__ residual,
+                             const __nv_bfloat16* __restrict__ w, float eps, int s_max, int T,
+                             int H, int64_t flag_off, uint32_t* __restrict__ gemm_epochs,
+                             uint32_t* __restrict__ epochs, int64_t timeout_ns, int* status) {
+  const uint32_t want = gemm_epochs[blockIdx.x] + 1;
+  __shared__ int ok;
+  __shared__ float red[33];
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < k) {
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(P.base[rank] + flag_off) + threadIdx.x;
+    const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(timeout_ns);
+    while (static_cast<int32_t>(ld_acquire_sys(f) - want) < 0) {
+      if (globaltimer_ns() > deadline) {
+        set_status(status, kErrPeerTimeout, 220);
+        atomicExch(&ok, 0);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int lo = static_cast<int>(int64_t(T) * rank / k), hi = static_cast<int>(int64_t(T) * (rank + 1) / k);
+  const int hv = H / 8;
+  for (int row = blockIdx.x; row < hi - lo; row += gridDim.x) {
+    float v[4][8];
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = threadIdx.x + j * blockDim.x;
+      if (col >= hv) continue;
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int r = 0; r < k; ++r) {
+        uint4 x = __ldcg(reinterpret_cast<const uint4*>(P.base[rank] + in_off) +
+                         (int64_t(r) * s_max + row) * hv + col);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f = __bfloat1622float2(h[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+      float rr[8];
+      load8(residual + (int64_t(lo) + row) * H + col * 8, rr);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float sum = __bfloat162float(__float2bfloat16(acc[e]));  // the reduced output, bf16
+        v[j][e] = __bfloat162float(__float2bfloat16(sum + rr[e]));  // new residual, bf16
+        s2 += v[j][e] * v[j][e];
+      }
+    }
+    const float scale = rsqrtf(block_sum(s2, red) / H + eps);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = threadIdx.x + j * blockDim.x;
+      if (col >= hv) continue;
+      float wf[8], o[8];
+      load8(w + col * 8, wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[j][e] * scale * wf[e];
+      uint4 ov, rv;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&ov);
+      __nv_bfloat162* rh = reinterpret_cast<__nv_bfloat162*>(&rv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        oh[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+        rh[e] = __floats2bfloat162_rn(v[j][2 * e], v[j][2 * e + 1]);
+      }
+      const int64_t idx = (int64_t(lo) + row) * hv + col;
+      for (int p = 0; p < k; ++p) {
+        const int q = (rank + p) % k;
+        reinterpret_cast<uint4*>(P.base[q] + out_off)[idx] = ov;
+        reinterpret_cast<uint4*>(P.base[q] + res_off)[idx] = rv;
+      }
+    }
+  }
+  const uint32_t epoch = epochs[blockIdx.x] + 1;
+  if (!block_barrier(P, rank, k, 1, epoch, timeout_ns, status)) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    epochs[blockIdx.x] = epoch;
+    gemm_epochs[blockIdx.x] = want;
+  }
+}
+
+void tp_rs_finish_norm(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
+                       int64_t res_off, torch::Tensor residual, torch::Tensor w, double eps,
+                       int64_t s_max, int64_t T, int64_t H, int64_t flag_off,
+                       torch::Tensor gemm_epochs, torch::Tensor epochs, double timeout_s) {
+  const int k = static_cast<int>(bases.size());
+  TORCH_CHECK(k >= 2 && k <= kArMaxRanks);
+  CHECK_BF16(residual);
+  CHECK_BF16(w);
+  TORCH_CHECK(residual.is_contiguous() && residual.numel() >= T * H && w.numel() == H);
+  TORCH_CHECK(H % 8 == 0 && H <= 4 * 8 * kArThreads, "tp_rs_finish_norm: H too large");
+  TORCH_CHECK(in_off % 16 == 0 && out_off % 16 == 0 && res_off % 16 == 0 && flag_off % 4 == 0);
+  TORCH_CHECK(epochs.numel() >= kArBlocks && gemm_epochs.numel() >= kArBlocks);
+  ArPeers P;
+  for (int r = 0; r < kArMaxRanks; ++r) P.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
+  tp_rs_finish_norm_kernel<<<kArBlocks, kArThreads, 0, cur_stream()>>>(
+      P, static_cast<int>(rank), k, in_off, out_off, res_off,
+      reinterpret_cast<const __nv_bfloat16*>(residual.data_ptr<at::BFloat16>()),
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>()), static_cast<float>(eps),
+      static_cast<int>(s_max), static_cast<int>(T), static_cast<int>(H), flag_off,
+      reinterpret_cast<uint32_t*>(gemm_epochs.data_ptr<int32_t>()),
+      reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>()),
+      static_cast<int64_t>(timeout_s * 1e9), status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+}
+
 // Test hook: one bounded wait on a flag nobody sets (single GPU, no peer):
 // must return with kErrPeerTimeout recorded, the context still usable.
 __global__ void flag_wait_probe_kernel(const uint32_t* flag, uint32_t want, int64_t timeout_ns,

@@ -75,6 +75,11 @@ class TPGroup:
             b = None
         return self.reduce(ops.linear(x, w, b))
 
+    def linear_reduce_norm(self, x: torch.Tensor, w: torch.Tensor, norm_w: torch.Tensor,
+                           eps: float, residual: torch.Tensor):
+        """linear_reduce, then residual add + RMSNorm: (normed, residual)."""
+        return ops.rms_norm(self.linear_reduce(x, w), norm_w, eps, residual)
+
 
 def _shard(n: int, rank: int, size: int):
     if n % size:
@@ -277,6 +282,18 @@ class DecoderModel:
             return self.tp.linear_reduce(a2, L.wo)
         return ops.linear(a2, L.wo)
 
+    def _attention_norm(self, i, L, x, meta, kv_cache, residual):
+        c = self.cfg
+        q = ops.qkv_rope_cache(ops.linear(x, L.wqkv), meta.positions, self.cos_sin, kv_cache, i,
+                               meta.slot_mapping, self.local_heads, self.local_kv_heads,
+                               c.head_dim, c.rotary_dim, L.bqkv)
+        a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
+        return self.tp.linear_reduce_norm(a.reshape(a.shape[0], -1), L.wo, L.ln2, c.rms_norm_eps,
+                                          residual)
+
+    def _mlp_hidden(self, L, x):
+        return ops.silu_and_mul(ops.linear(x, L.w13))
+
     def _reduce_slot(self, T: int):
         """Where a row-parallel GEMM should write its partial output: the
         fused TP backend hands out its NVLink-visible buffer (GEMM -> reduce
@@ -306,6 +323,8 @@ class DecoderModel:
         c = self.cfg
         h = ops.embedding(input_ids, self.embed)
         residual = None
+        fuse_norm = (self.tp.size > 1 and not c.parallel_block and not c.num_experts
+                     and c.norm_type != "layernorm" and not c.hidden_act.startswith("gelu"))
         for i, L in enumerate(self.layers):
             if c.parallel_block:
                 x, _ = self._norm(h, L.ln1, L.ln1_b)
@@ -319,6 +338,19 @@ class DecoderModel:
                         s = s + L.b2
                 s = self.tp.reduce(s)
                 h = h + s
+                continue
+            if fuse_norm:
+                # the row-parallel reduction also does the residual add and
+                # the RMSNorm that follows it (one kernel under fused TP)
+                if i == 0:
+                    x, residual = self._norm(h, L.ln1, L.ln1_b, None)
+                x, residual = self._attention_norm(i, L, x, meta, kv_cache, residual)
+                if i + 1 < len(self.layers):
+                    nxt = self.layers[i + 1]
+                    x, residual = self.tp.linear_reduce_norm(
+                        self._mlp_hidden(L, x), L.w2, nxt.ln1, c.rms_norm_eps, residual)
+                else:
+                    h = self._mlp(L, x)
                 continue
             x, residual = self._norm(h, L.ln1, L.ln1_b, residual)
             a = self._attention(i, L, x, meta, kv_cache)

@@ -40,6 +40,8 @@ log = get_logger(__name__)
 _FLAGS_BYTES = 64 << 10
 _GEMM_FLAG_OFF = 8 << 10
 FUSED_GEMM = os.environ.get("SWIFTLLM_FUSED_GEMM_RS", "1") == "1"
+# residual add + RMSNorm folded into the reduce's finish kernel
+FUSED_NORM = os.environ.get("SWIFTLLM_FUSED_NORM", "0") == "1"
 TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
 
 
@@ -58,7 +60,7 @@ class FusedTP(NcclTP):
         self.max_elems = max_tokens * H
         self.s_max = (max_tokens + size - 1) // size
         self.buf_bytes = ((max_tokens + 8) * H * 2 + 255) // 256 * 256
-        total = _FLAGS_BYTES + 4 * self.buf_bytes
+        total = _FLAGS_BYTES + 6 * self.buf_bytes
         self.symm = symm_mem.empty(total // 2, dtype=torch.bfloat16, device=device)
         self.symm.zero_()
         torch.cuda.synchronize(device)
@@ -74,7 +76,7 @@ class FusedTP(NcclTP):
                  total / 2**20)
 
     def _off(self, kind: str, parity: int) -> int:
-        base = _FLAGS_BYTES + (0 if kind == "in" else 2 * self.buf_bytes)
+        base = _FLAGS_BYTES + {"in": 0, "red": 2, "res": 4}[kind] * self.buf_bytes
         return base + parity * self.buf_bytes
 
     def reduce_buffer(self, T: int, H: int) -> Optional[torch.Tensor]:
@@ -125,6 +127,33 @@ class FusedTP(NcclTP):
         ops._count(n + 1)
         self.call += 1
         return self.symm[red_off // 2:red_off // 2 + T * H].view(T, H)
+
+    def linear_reduce_norm(self, x: torch.Tensor, w: torch.Tensor, norm_w: torch.Tensor,
+                           eps: float, residual: torch.Tensor):
+        """Row-parallel linear, cross-rank sum, residual add and RMSNorm:
+        returns (normed, new residual) like ``ops.rms_norm(out, norm_w, eps,
+        residual)``. Fused path: the GEMM -> reduce-scatter kernel, then one
+        kernel that reduces each rank's own tokens, adds the residual,
+        normalises and all-gathers both rows."""
+        from .. import ops
+        T, H = x.shape[0], w.shape[0]
+        if (not (FUSED_GEMM and FUSED_NORM) or not isinstance(w, torch.Tensor) or x.shape[-1] % 8
+                or T == 0 or T > self.max_tokens or H != self.H or ops.gemm_backend() != "tcgen05"
+                or not residual.is_contiguous()):
+            return ops.rms_norm(self.linear_reduce(x, w), norm_w, eps, residual)
+        parity = self.call % 2
+        in_off, out_off, res_off = (self._off("in", parity), self._off("red", parity),
+                                    self._off("res", parity))
+        n = self.C.gemm_rs(x, w, None, self.bases, self.rank, in_off, self.s_max, _GEMM_FLAG_OFF,
+                           self.gemm_ctr)
+        self.C.tp_rs_finish_norm(self.bases, self.rank, in_off, out_off, res_off, residual, norm_w,
+                                 float(eps), self.s_max, T, H, _GEMM_FLAG_OFF, self.gemm_epochs,
+                                 self.epochs, TIMEOUT_S)
+        ops._count(n + 1)
+        self.call += 1
+        normed = self.symm[out_off // 2:out_off // 2 + T * H].view(T, H)
+        res = self.symm[res_off // 2:res_off // 2 + T * H].view(T, H)
+        return normed, res
 
     def check(self) -> None:
         st = self.C.read_status(True)

@@ -65,6 +65,19 @@ def main():
             for fused in (True, False):
                 got = tp.linear_reduce(x, w, fused=fused)
                 torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=3e-2)
+            # + residual add + RMSNorm in the finish kernel
+            res = torch.randn(T, H, device=dev, generator=g).to(dtype)
+            dist.broadcast(res, 0)
+            nw = (torch.rand(H, device=dev, generator=g) + 0.5).to(dtype)
+            dist.broadcast(nw, 0)
+            r_ref = (ref.to(dtype).float() + res.float()).to(dtype).float()
+            n_ref = r_ref * torch.rsqrt(r_ref.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float()
+            import swiftllm_b200.parallel.fused_comm as fc
+            for on in (True, False):
+                fc.FUSED_NORM = on
+                got_n, got_r = tp.linear_reduce_norm(x, w, nw, 1e-5, res.clone())
+                torch.testing.assert_close(got_r.float(), r_ref, rtol=2e-2, atol=3e-2)
+                torch.testing.assert_close(got_n.float(), n_ref, rtol=3e-2, atol=3e-2)
         st = tp.C.read_status(True)
         assert st[0] == 0, st
     m = DecoderModel(cfg, dtype, dev, tp)
