@@ -213,47 +213,89 @@ def reference_arm(args) -> None:
         print(json.dumps({"impl": "reference", "unavailable": msg}))
 
 
-def main() -> None:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--requests", type=int, default=None)
-    ap.add_argument("--model", default=None)
-    ap.add_argument("--workload", default="llama2-7b", choices=sorted(WORKLOADS))
-    ap.add_argument("--max-num-seqs", type=int, default=None)
-    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
-    ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
-    ap.add_argument("--profile-host", action="store_true",
-                    help="report host phases and the GPU idle gap between steps (diagnostic)")
-    args = ap.parse_args()
-    wl = WORKLOADS[args.workload]
-    args.model = args.model or wl["model"]
-    args.requests = args.requests or wl["requests"]
-    args.max_num_seqs = args.max_num_seqs or wl["max_num_seqs"]
-    if args.impl == "reference":
-        reference_arm(args)
-        return
-    args.warmup = max(args.warmup, 3)
-    os.environ["SWIFTLLM_GEMM"] = args.gemm
-    import torch
-    from swiftllm_b200 import LLM, SamplingParams
-    from swiftllm_b200.config import EngineConfig
-    from swiftllm_b200 import ops
+def _model_bytes(mcfg) -> int:
+    """bf16 bytes of the full (single-rank) model."""
+    H, D, L = mcfg.hidden_size, mcfg.head_dim, mcfg.num_layers
+    qkv = (mcfg.num_heads + 2 * mcfg.num_kv_heads) * D * H
+    o = mcfg.num_heads * D * H
+    mlp = 3 * mcfg.intermediate_size * H * max(1, mcfg.num_experts or 1)
+    return 2 * (L * (qkv + o + mlp) + 2 * mcfg.vocab_size * H)
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    if world != args.gpus:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+
+CHECK_LEN = 48   # prompt tokens of the TP logits check
+CHECK_ROWS = 8   # last rows whose logits are compared
+
+
+def tp_reference_logits(model: str, ekw: dict):
+    """Rank 0, before the TP engine exists: the same dummy-initialised model
+    on one GPU (no tensor parallelism, cuBLAS GEMMs) runs a CHECK_LEN-token
+    prefill and returns the fp32 logits of its last CHECK_ROWS positions, or
+    None when the model does not fit one GPU comfortably."""
+    import torch
+    from swiftllm_b200 import ops
+    from swiftllm_b200.config import EngineConfig
+    from swiftllm_b200.engine.llm_engine import prepare_config
+    from swiftllm_b200.runtime.model_runner import ModelRunner, prefill_step_input
+    cfg = EngineConfig(model=model, **dict(ekw, tensor_parallel_size=1))
+    mcfg = prepare_config(cfg)
+    if _model_bytes(mcfg) > 0.4 * torch.cuda.get_device_properties(0).total_memory:
+        return None, None
+    ops.set_gemm_backend("cublas")
+    runner = ModelRunner(mcfg, cfg, torch.device("cuda", torch.cuda.current_device()), None,
+                         cfg.max_model_len)
+    runner.load_weights()
+    ids = np.random.default_rng(1).integers(0, mcfg.vocab_size, size=CHECK_LEN).tolist()
+    si = prefill_step_input(ids, cfg.block_size, CHECK_ROWS)
+    runner.allocate_kv(si.max_blocks + 1, 0)
+    logits = runner.execute(si).float().cpu()
+    runner.release()
+    ops.set_gemm_backend(ops.DEFAULT_GEMM_BACKEND)
+    return ids, logits
+
+
+def tp_logits_check(eng, ids, ref) -> dict:
+    """One prefill step of the check prompt through the TP engine's executor
+    (every rank runs it; blocks 0.. are free before any request) compared
+    with the single-GPU logits."""
+    import torch
+    from swiftllm_b200.runtime.model_runner import prefill_step_input
+    si = prefill_step_input(ids, eng.config.block_size, CHECK_ROWS)
+    got = eng.executor.execute(si).float().cpu()
+    err = (got - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(got, ref, dim=-1).min().item()
+    agree = (got.argmax(-1) == ref.argmax(-1)).float().mean().item()
+    return {"vs": "tp1 single-GPU forward, same weights", "rows": CHECK_ROWS,
+            "max_abs_err": round(err, 4), "ref_max_abs": round(scale, 4),
+            "min_cosine": round(cos, 6), "argmax_agree": round(agree, 3),
+            "ok": bool(cos > 0.999 and err < 0.05 * max(scale, 1e-6))}
+
+
+def run_arm(args, wl, arm: str, rank: int, check=None):
+    """One full run of the workload through LLM.generate with the given
+    backend arm ("ours": tcgen05 GEMMs + fused NVLink reductions; "baseline":
+    cuBLAS GEMMs + NCCL all-reduce, the same engine otherwise). Returns the
+    result dict on rank 0, None on the other ranks. Leaves no device memory
+    of the engine behind."""
+    import gc
+    import torch
+    from swiftllm_b200 import LLM, SamplingParams, ops
+    from swiftllm_b200.config import EngineConfig
+    comm = args.comm if arm == "ours" else "nccl"
     ekw = dict(load_format="dummy", dtype="bfloat16", tensor_parallel_size=args.gpus,
                gpu_memory_utilization=0.9, block_size=16, max_num_seqs=args.max_num_seqs,
-               enable_chunked_prefill=True, max_num_batched_tokens=8192, max_model_len=wl["max_model_len"],
-               comm_backend=args.comm, seed=0, preemption_mode="recompute")
+               enable_chunked_prefill=True, max_num_batched_tokens=8192,
+               max_model_len=wl["max_model_len"], comm_backend=comm, seed=0,
+               preemption_mode="recompute")
+    os.environ["SWIFTLLM_CHANNEL"] = f"/swiftllm-bench-{os.environ.get('MASTER_PORT', '0')}-{arm}"
+    if arm == "ours":
+        ops.set_gemm_backend(args.gemm)
     if rank != 0:
         from swiftllm_b200.parallel.executor import run_worker_from_env
         run_worker_from_env(EngineConfig(model=args.model, **ekw))
-        _exit_now()
+        gc.collect()
+        torch.cuda.empty_cache()
+        return None
 
     prompts, out_lens = workload(args.requests, 0, wl["ins"], wl["outs"], wl["vocab"])
     sps = [SamplingParams(temperature=0.0, max_tokens=o, ignore_eos=True) for o in out_lens]
@@ -262,6 +304,7 @@ def main() -> None:
     eng = llm.llm_engine
     eng._ensure_initialized()
     init_s = time.time() - t_init
+    check_res = tp_logits_check(eng, check[0], check[1]) if check is not None else None
     clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")))
     st = {"filled": None, "start": None, "stop": None, "tok": 0, "launch0": 0, "launches": 0}
 
@@ -283,7 +326,7 @@ def main() -> None:
                 st["launches"] = ops.LAUNCHES[0] - st["launch0"]
 
     eng.step_hook = hook
-    prof = HostProfile(eng) if args.profile_host else None
+    prof = HostProfile(eng) if args.profile_host and arm == "ours" else None
     torch.cuda.synchronize()
     io_before = list(eng.io_bytes)
     steps_before = eng.num_steps
@@ -305,34 +348,11 @@ def main() -> None:
     tpot = [o.metrics["tpot"] for o in outs if o.metrics and o.metrics["tpot"] is not None]
     timed_steps = (st["stop"] - st["start"]) if st["start"] is not None else 0
     value = st["tok"] / (ms / 1e3) if ms else None
-    e2e_value = n_out / e2e_s
     res = {
-        "metric": METRIC,
         "value": round(value, 1) if value else None,
-        "unit": "output tokens/s",
-        "n_gpus": args.gpus,
-        "steps": timed_steps,
-        "warmup": args.warmup,
         "ms_per_step": round(ms / max(timed_steps, 1), 3) if ms else None,
-        "higher_is_better": True,
-        "scaling": "strong",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
-        "config": {
-            "model": wl["desc"],
-            "workload": args.workload,
-            "global_batch": args.max_num_seqs,
-            "seq_len": f"in U[{wl['ins'][0]},{wl['ins'][1]}], out U[{wl['outs'][0]},{wl['outs'][1]}]",
-            "requests": args.requests,
-            "parallelism": f"tp{args.gpus}",
-            "comm": args.comm if args.gpus > 1 else "none",
-            "gemm": args.gemm,
-            "l2": "no flush: each step streams weights + KV pool (>126 MB L2)",
-            "window": f"{timed_steps} engine steps starting {args.warmup} steps after the batch "
-                      f"first filled to {args.max_num_seqs} running sequences",
-        },
-        "e2e": {"value": round(e2e_value, 1),
+        "steps": timed_steps,
+        "e2e": {"value": round(n_out / e2e_s, 1),
                 "unit": "output tokens/s (LLM.generate, whole workload)",
                 "seconds": round(e2e_s, 2), "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "engine_steps": steps_total,
@@ -343,20 +363,113 @@ def main() -> None:
         "clocks": clk,
         "init_s": round(init_s, 1),
     }
+    if check_res is not None:
+        res["tp_check"] = check_res
     if prof is not None:
         res["host_profile"] = prof.report()
-    print(json.dumps(res), flush=True)
     llm.shutdown()
-    _exit_now()
+    del llm, eng, outs
+    gc.collect()
+    torch.cuda.empty_cache()
+    return res
 
 
-def _exit_now() -> None:
-    """Leave without running library teardown: the result is printed and
-    flushed, the workers are shut down, and NCCL / symmetric-memory
-    destructors at interpreter exit have aborted some multi-rank runs."""
-    sys.stdout.flush()
-    sys.stderr.flush()
-    os._exit(0)
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--requests", type=int, default=None)
+    ap.add_argument("--model", default=None)
+    ap.add_argument("--workload", default="llama2-7b", choices=sorted(WORKLOADS))
+    ap.add_argument("--max-num-seqs", type=int, default=None)
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
+    ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
+    ap.add_argument("--baseline", default="run", choices=["run", "skip"],
+                    help="also run the cuBLAS + NCCL arm on the same workload (vs_baseline)")
+    ap.add_argument("--profile-host", action="store_true",
+                    help="report host phases and the GPU idle gap between steps (diagnostic)")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    args.model = args.model or wl["model"]
+    args.requests = args.requests or wl["requests"]
+    args.max_num_seqs = args.max_num_seqs or wl["max_num_seqs"]
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    args.warmup = max(args.warmup, 3)
+    os.environ["SWIFTLLM_GEMM"] = args.gemm
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun")
+    if world > 1:
+        from swiftllm_b200.parallel.comm import init_distributed
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
+        init_distributed(rank, world, "nccl")
+    check = None
+    if world > 1 and rank == 0:
+        ids, ref = tp_reference_logits(args.model, dict(
+            load_format="dummy", dtype="bfloat16", block_size=16, max_num_seqs=CHECK_ROWS,
+            enable_chunked_prefill=True, max_num_batched_tokens=8192,
+            max_model_len=wl["max_model_len"], seed=0, enforce_eager=True))
+        check = (ids, ref) if ids is not None else None
+    arms = ["baseline", "ours"] if args.baseline == "run" else ["ours"]
+    results = {arm: run_arm(args, wl, arm, rank, check if arm == "ours" else None) for arm in arms}
+    if rank == 0:
+        r, b = results["ours"], results.get("baseline")
+        vs = (round(r["value"] / b["value"], 3) if b and b.get("value") and r.get("value")
+              else None)
+        res = {
+            "metric": METRIC,
+            "value": r["value"],
+            "unit": "output tokens/s",
+            "n_gpus": args.gpus,
+            "steps": r["steps"],
+            "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": vs,
+            "dtype": "bf16",
+            "data": "synthetic (uniform random token ids, random-init N(0,0.02) weights)",
+            "config": {
+                "model": wl["desc"],
+                "workload": args.workload,
+                "global_batch": args.max_num_seqs,
+                "seq_len": f"in U[{wl['ins'][0]},{wl['ins'][1]}], out U[{wl['outs'][0]},{wl['outs'][1]}]",
+                "requests": args.requests,
+                "parallelism": f"tp{args.gpus}",
+                "comm": args.comm if args.gpus > 1 else "none",
+                "gemm": args.gemm,
+                "l2": "no flush: each step streams weights + KV pool (>126 MB L2)",
+                "window": f"{r['steps']} engine steps starting {args.warmup} steps after the batch "
+                          f"first filled to {args.max_num_seqs} running sequences",
+                "baseline_arm": "same engine and workload with cuBLAS GEMMs (torch.matmul) and "
+                                "NCCL all-reduce / all-gather, run first in this process",
+            },
+            "e2e": r["e2e"],
+            "p50_ttft_ms": r["p50_ttft_ms"],
+            "p50_tpot_ms": r["p50_tpot_ms"],
+            "gpu_launches": r["gpu_launches"],
+            "clocks": r["clocks"],
+            "init_s": r["init_s"],
+        }
+        if b is not None:
+            res["baseline"] = {k: b[k] for k in ("value", "ms_per_step", "e2e", "p50_ttft_ms",
+                                                 "p50_tpot_ms", "clocks")}
+            res["e2e_vs_baseline"] = (round(r["e2e"]["value"] / b["e2e"]["value"], 3)
+                                      if b["e2e"]["value"] else None)
+        for k in ("tp_check", "host_profile"):
+            if k in r:
+                res[k] = r[k]
+        print(json.dumps(res), flush=True)
+    if world > 1:
+        from swiftllm_b200.parallel.comm import teardown_distributed
+        teardown_distributed()
 
 
 if __name__ == "__main__":

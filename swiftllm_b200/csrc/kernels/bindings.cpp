@@ -32,7 +32,7 @@ void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch
             torch::Tensor iparams, torch::Tensor keys, bool any_random);
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
-torch::Tensor gemm_sk_stamps();
+void gemm_streamk_config(int64_t mode, int64_t mt, int64_t min_per);
 void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x);
 int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
                   torch::Tensor wscale, c10::optional<torch::Tensor> bias);
@@ -78,7 +78,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &swift::sample);
   m.def("gemm", &swift::gemm);
   m.def("gemm_plan", &swift::gemm_plan);
-  m.def("gemm_sk_stamps", &swift::gemm_sk_stamps);
+  m.def("gemm_streamk_config", &swift::gemm_streamk_config);
   m.def("gemm_packed", &swift::gemm_packed);
   m.def("gemm_rs", &swift::gemm_rs);
   m.def("gemm_e4m3", &swift::gemm_e4m3);

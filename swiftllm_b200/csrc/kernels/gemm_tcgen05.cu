@@ -512,8 +512,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
                         int64_t ldy, const __nv_bfloat16* __restrict__ bias,
                         float* __restrict__ ws, int* __restrict__ counters, int M, int N, int K,
-                        int per, int* status, int probe, int vec_out,
-                        unsigned long long* __restrict__ stamps, int packed_kt, int rot_mul,
+                        int per, int* status, int vec_out, int packed_kt,
                         const ScatterDesc sc) {
   using S = SkSmem<BN, MT, STAGES>;
   constexpr int UM = S::UM, NBUF = S::NBUF;
@@ -562,17 +561,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // measurement probe bit 4: epilogue thread 64 records %globaltimer at phase
-  // boundaries (kernel start, per segment: accumulator ready, partial
-  // stored, done) into stamps[cta][16]
-  auto stamp = [&](int k) {
-    if ((probe & 4) && threadIdx.x == 64 && k < 16) {
-      unsigned long long t;
-      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-      stamps[cta * 16 + k] = t;
-    }
-  };
-  stamp(0);
 
   // Segments of this CTA's range, natural order j = 0..nseg-1 (tile
   // first_tile + j). Processing order: a partial LAST segment goes first
@@ -598,24 +586,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int j, t, k0, k1;
         seg_of(p, j, t, k0, k1);
         const int w0 = (t / n_tiles) * UM, x0 = (t % n_tiles) * BN;
-        const int len = k1 - k0, rot = rot_mul ? (cta * rot_mul) % len : 0;
-        for (int kq = k0; kq < k1; ++kq, ++it) {
-          // optional rotation of the K order per CTA (measurement knob)
-          const int kk = rot ? k0 + (kq - k0 + rot) % len : kq;
+        for (int kk = k0; kk < k1; ++kk, ++it) {
           const int st = it % STAGES;
           if (!wait_or_abort(&empty[st], ((it / STAGES) & 1) ^ 1, abort_flag, status, 20)) {
             ok = false;
             break;
           }
           uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
-          if ((probe & 3) == 2) {  // measurement probe: no loads (tensor-pipe time alone)
-            mbar_arrive(&full[st]);
-            continue;
-          }
-          // probe bits 16 / 32 (measurement): skip the weight / token loads
-          mbar_arrive_expect_tx(&full[st], (probe & 16 ? 0 : S::A_BYTES) + (probe & 32 ? 0 : S::B_BYTES));
-          if (probe & 16) {
-          } else if (packed_kt) {  // tile-packed weights: one contiguous 16 KB box per 128 rows
+          mbar_arrive_expect_tx(&full[st], S::STAGE_BYTES);
+          if (packed_kt) {  // tile-packed weights: one contiguous 16 KB box per 128 rows
 #pragma unroll
             for (int mi = 0; mi < MT; ++mi)
               tma_load_2d(a + mi * kGemmBM * kGemmBK * 2, &tm_w, 0,
@@ -623,7 +602,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             tma_load_2d(a, &tm_w, kk * kGemmBK, w0, &full[st]);
           }
-          if (!(probe & 32)) tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, x0, &full[st]);
+          tma_load_2d(a + S::A_BYTES, &tm_x, kk * kGemmBK, x0, &full[st]);
         }
       }
       if (!ok) {
@@ -658,7 +637,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
 #pragma unroll
           for (int q = 0; q < kGemmBK / 16; ++q) {
-            if ((probe & 3) == 1) break;  // measurement probe: no MMAs (load time alone)
 #pragma unroll
             for (int i = 0; i < MT; ++i) {
               const uint64_t ad = smem_desc_sw128(a + i * kGemmBM * kGemmBK * 2);
@@ -706,10 +684,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       ok = sh_ok[tc & 1][0] && sh_ok[tc & 1][1] && sh_ok[tc & 1][2] && sh_ok[tc & 1][3];
       if (!ok) break;
       tc_fence_after();
-      stamp(1 + 3 * p);
-      // probe bit 64 (measurement, wrong results): every segment treated as
-      // a whole tile (no partials, no fix-up)
-      const bool whole = (k0 == 0 && k1 == k_iters) || (probe & 64);
+      const bool whole = k0 == 0 && k1 == k_iters;
       const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * S::ACC_COLS;
       const int fl = q * 32 + lane;  // feature within a 128-row sub-tile
       bool last = whole;
@@ -760,13 +735,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           epi_bar();
           last = sh_last != 0;
         }
-        stamp(2 + 3 * p);
       }
       // The CTA's last processed segment: producer and MMAs are done, so the
       // other CTAs' partials are fetched with bulk copies into the idle
       // shared-memory ring (one latency instead of one per chunk).
       const int others = whole ? 0 : cl - cf;
-      const bool staged = last && others > 0 && p == nseg - 1 && !(probe & 8) &&
+      const bool staged = last && others > 0 && p == nseg - 1 &&
                           size_t(others) * slot_floats * 4 <= size_t(STAGES) * S::STAGE_BYTES;
       if (staged) {
         if (threadIdx.x == 64) {
@@ -828,9 +802,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               ++idx;
             }
             const int t0 = x0 + c * 32;
-            if (probe & 128) {  // measurement: no output stores
-              if (v[0] == 12345.f) y[0] = __float2bfloat16(v[1]);
-            } else if (vec_out) {
+            if (vec_out) {
               // transpose through shared memory: 4 lanes write one token's
               // 32 features as 16-byte vectors
 #pragma unroll
@@ -856,7 +828,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      stamp(3 + 3 * p);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
@@ -865,7 +836,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   sc_publish(sc);
-  stamp(15);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -957,7 +927,6 @@ static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloa
 struct SkBuffers {
   float* ws = nullptr;
   int* counters = nullptr;
-  unsigned long long* stamps = nullptr;  // probe 3 timestamps [grid][16]
 };
 constexpr int kSkMaxTiles = 8192;
 constexpr size_t kSkSlotFloats = 256 * 256;  // UM * BN at most
@@ -972,16 +941,34 @@ static SkBuffers& sk_buffers() {
     SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].ws, size_t(2) * num_sms() * kSkSlotFloats * sizeof(float)));
     SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].counters, kSkMaxTiles * sizeof(int)));
     SWIFT_CHECK_CUDA(cudaMemset(b[dev].counters, 0, kSkMaxTiles * sizeof(int)));
-    SWIFT_CHECK_CUDA(cudaMalloc(&b[dev].stamps, 256 * 16 * sizeof(unsigned long long)));
-    SWIFT_CHECK_CUDA(cudaMemset(b[dev].stamps, 0, 256 * 16 * sizeof(unsigned long long)));
     SWIFT_CHECK_CUDA(cudaDeviceSynchronize());
   }
   return b[dev];
 }
 
-static int env_int(const char* name, int dflt) {
-  const char* v = std::getenv(name);
-  return v && *v ? std::atoi(v) : dflt;
+// Stream-K planning parameters, process wide. mode: 1 (default) stream-K
+// where the plan below picks it, 0 never, 2 for every shape it supports
+// (initial value from SWIFT_GEMM_STREAMK, read once); mt: 128-row feature
+// sub-tiles per unit (1 or 2); min_per: fewest k-iterations per CTA. Only
+// gemm_streamk_config() changes them (tests force split tiles with it).
+struct SkConfig {
+  int mode = -1, mt = 1, min_per = 32;
+};
+static SkConfig& sk_config() {
+  static SkConfig c;
+  if (c.mode < 0) {
+    const char* v = std::getenv("SWIFT_GEMM_STREAMK");
+    c.mode = v && *v ? std::atoi(v) : 1;
+  }
+  return c;
+}
+
+void gemm_streamk_config(int64_t mode, int64_t mt, int64_t min_per) {
+  TORCH_CHECK(mode >= 0 && mode <= 2 && (mt == 1 || mt == 2) && min_per >= 1);
+  SkConfig& c = sk_config();
+  c.mode = static_cast<int>(mode);
+  c.mt = static_cast<int>(mt);
+  c.min_per = static_cast<int>(min_per);
 }
 
 template <int BN, int MT>
@@ -1010,10 +997,8 @@ static void launch_sk(const void* w, int64_t ldw, const void* x, int64_t ldx, __
                        : make_tmap(w, M, K, ldw, S::UM);
   CUtensorMap tx = make_tmap(x, N, K, ldx, BN);
   kern<<<grid, kGemmThreads, S::BYTES, cur_stream()>>>(tw, tx, y, ldy, bias, b.ws, b.counters, M,
-                                                       N, K, per, status_word_ptr(),
-                                                       env_int("SWIFT_SK_PROBE", 0), vec_out,
-                                                       b.stamps, packed_kt,
-                                                       env_int("SWIFT_SK_ROT", 0), sc);
+                                                       N, K, per, status_word_ptr(), vec_out,
+                                                       packed_kt, sc);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -1031,7 +1016,8 @@ static void plan(int M, int N, int K, int* bn, int* splits);
 // served from L2). At least 32 k-iterations per CTA.
 static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per,
                     bool force = false) {
-  const int mode = force ? 2 : env_int("SWIFT_GEMM_STREAMK", 1);
+  const SkConfig& cfg = sk_config();
+  const int mode = force ? 2 : cfg.mode;
   if (N > 2048 || mode == 0) return false;
   const int sms = num_sms();
   if (mode == 1 && N > 256) {
@@ -1051,17 +1037,14 @@ static bool sk_plan(int M, int N, int K, int* bn, int* mt, int* grid, int* per,
   } else if (b == 256 && int64_t((M + kGemmBM - 1) / kGemmBM) * 2 <= int64_t(2) * sms) {
     b = 128;
   }
-  const int bo = env_int("SWIFT_SK_BN", 0);  // tuning override: narrower token tiles
-  if (bo == 32 || bo == 64 || bo == 128) b = std::min(b, bo);
   const int k_iters = (K + kGemmBK - 1) / kGemmBK;
-  int m = env_int("SWIFT_SK_MT", 0);
-  if (m != 1 && m != 2) m = 1;
+  const int m = cfg.mt;
   const int units = (M + 128 * m - 1) / (128 * m) * ((N + b - 1) / b);
   if (units > kSkMaxTiles) return false;
   const int64_t total = int64_t(units) * k_iters;
   // at least 32 k-iterations per CTA, but never more than one tile's worth
   // (short K: one CTA per tile keeps every tile's CTA busy)
-  const int min_per = std::max(1, std::min(env_int("SWIFT_SK_MINPER", 32), k_iters));
+  const int min_per = std::max(1, std::min(cfg.min_per, k_iters));
   int g = static_cast<int>(std::min<int64_t>(sms, (total + min_per - 1) / min_per));
   g = std::max(g, 1);
   int p = static_cast<int>((total + g - 1) / g);
@@ -1197,10 +1180,8 @@ int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> b
   sc.s_max = static_cast<int>(s_max);
   sc.T = static_cast<int>(T);
   sc.H = static_cast<int>(H);
-  // every thread fences its remote stores before the CTA publishes
-  // (SWIFT_RS_FENCE_ALL=0: only thread 0 after bar.sync, the split-K
-  // semaphore pattern, which relies on the fence's cumulativity)
-  sc.fence_all = env_int("SWIFT_RS_FENCE_ALL", 1);
+  // every thread fences its own remote stores before the CTA publishes
+  sc.fence_all = 1;
   if (T == 0) return 0;
   return gemm_impl(nullptr, 0, x, w, bias, sc);
 }
@@ -1317,16 +1298,6 @@ int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, tor
     return 2;
   }
   return 1;
-}
-
-// Timestamps of the last stream-K launch made with SWIFT_SK_PROBE bit 4 set
-// ([256, 16] int64 nanoseconds; 0 = not reached), for kernel phase timing.
-torch::Tensor gemm_sk_stamps() {
-  SkBuffers& b = sk_buffers();
-  auto t = torch::empty({256, 16}, torch::dtype(torch::kInt64));
-  SWIFT_CHECK_CUDA(cudaMemcpy(t.data_ptr(), b.stamps, 256 * 16 * 8, cudaMemcpyDeviceToHost));
-  SWIFT_CHECK_CUDA(cudaMemset(b.stamps, 0, 256 * 16 * 8));
-  return t;
 }
 
 // [token tile, splits, stream-K features-per-unit / 128 (0: not stream-K),

@@ -229,11 +229,9 @@ void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int6
   TORCH_CHECK(gemm_epochs.scalar_type() == at::kInt && gemm_epochs.numel() >= kArBlocks);
   ArPeers P;
   for (int r = 0; r < kArMaxRanks; ++r) P.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
-  // blocks of the finish kernel (fewer blocks = fewer flags per barrier
-  // round); SWIFT_RS_BLOCKS tunes it
-  const char* eb = std::getenv("SWIFT_RS_BLOCKS");
-  const int blocks = std::max(1, std::min(kArBlocks, eb && *eb ? std::atoi(eb) : kArBlocks));
-  tp_rs_finish_kernel<<<blocks, kArThreads, 0, cur_stream()>>>(
+  // every finish kernel runs kArBlocks blocks: block b owns the per-block
+  // epoch counters b of gemm_epochs / epochs, shared by all of them
+  tp_rs_finish_kernel<<<kArBlocks, kArThreads, 0, cur_stream()>>>(
       P, static_cast<int>(rank), k, in_off, out_off, static_cast<int>(s_max), static_cast<int>(T),
       static_cast<int>(H), flag_off, reinterpret_cast<uint32_t*>(gemm_epochs.data_ptr<int32_t>()),
       reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>()),

@@ -36,7 +36,8 @@ def has_cuda_ext() -> bool:
 
 # GEMM backend for CUDA tensors: "tcgen05" (our kernel, default) or "cublas"
 # (torch.matmul; only the NCCL+cuBLAS baseline path selects it).
-_GEMM_BACKEND = os.environ.get("SWIFTLLM_GEMM", "tcgen05")
+DEFAULT_GEMM_BACKEND = os.environ.get("SWIFTLLM_GEMM", "tcgen05")
+_GEMM_BACKEND = DEFAULT_GEMM_BACKEND
 
 
 def set_gemm_backend(name: str) -> None:

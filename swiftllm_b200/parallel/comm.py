@@ -41,6 +41,22 @@ def init_distributed(rank: int, world: int, backend: str) -> None:
     dist.init_process_group(backend=backend, rank=rank, world_size=world, **kwargs)
 
 
+def teardown_distributed() -> None:
+    """Orderly end of a multi-rank job: every rank calls this after its
+    engine / worker released its device buffers; a barrier makes sure no
+    peer still reads them, then the process group is destroyed so the
+    interpreter exits normally."""
+    import torch.distributed as dist
+    if not dist.is_initialized():
+        return
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    try:
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
 class NcclTP(TPGroup):
     """torch.distributed collectives (NCCL on GPUs, gloo on CPU)."""
 

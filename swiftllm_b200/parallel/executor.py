@@ -51,9 +51,12 @@ def _build_runner(model_cfg, cfg, rank: int, world: int, local_rank: int):
     device = _device_for(cfg, local_rank)
     tp = build_tp_group(rank, world, device, cfg.comm_backend, model_cfg,
                         max(int(cfg.max_num_batched_tokens or 8192), 16384))
-    if cfg.comm_backend == "nccl" and device.type == "cuda":
+    if device.type == "cuda":
+        # the NCCL backend is the library baseline: cuBLAS GEMMs + NCCL
+        # all-reduce; otherwise the process default (tcgen05 unless
+        # SWIFTLLM_GEMM says otherwise)
         from .. import ops
-        ops.set_gemm_backend("cublas")
+        ops.set_gemm_backend("cublas" if cfg.comm_backend == "nccl" else ops.DEFAULT_GEMM_BACKEND)
     runner = ModelRunner(model_cfg, cfg, device, tp, cfg.max_model_len)
     runner.load_weights()
     n = runner.profile_num_blocks()
@@ -96,11 +99,15 @@ def worker_loop(model_cfg, cfg, rank: int, world: int, local_rank: int, channel_
             _timer_op(runner, obj[1])
             continue
         runner.execute(obj)
+    del ch
+    runner.release()
 
 
 def run_worker_from_env(cfg) -> None:
     """Entry for ranks != 0 of a torchrun job (bench.py): join the process
-    group, build this rank's runner and serve rank 0's steps until shutdown."""
+    group, build this rank's runner and serve rank 0's steps until shutdown.
+    Returns after rank 0's shutdown with this rank's device memory released
+    (the process group stays up for a later engine or the final teardown)."""
     from ..engine.llm_engine import prepare_config
     model_cfg = prepare_config(cfg)
     rank = int(os.environ["RANK"])
@@ -257,6 +264,9 @@ class LocalExecutor:
                     p.terminate()
             self.channel.close()
             self.channel = None
+        if self.runner is not None:
+            self.runner.release()
+            self.runner = None
 
 
 def _free_port() -> int:

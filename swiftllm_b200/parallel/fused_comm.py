@@ -155,6 +155,18 @@ class FusedTP(NcclTP):
         res = self.symm[res_off // 2:res_off // 2 + T * H].view(T, H)
         return normed, res
 
+    def close(self) -> None:
+        """Release the symmetric allocation and its rendezvous handle (every
+        rank calls this between steps, then a barrier, before the process
+        group is destroyed)."""
+        if getattr(self, "symm", None) is None:
+            return
+        torch.cuda.synchronize(self.device)
+        self.hdl = None
+        self.bases = []
+        self.symm = None
+        self.epochs = self.gemm_ctr = self.gemm_epochs = None
+
     def check(self) -> None:
         st = self.C.read_status(True)
         if st[0] == 2:

@@ -70,6 +70,20 @@ def step_input_from_batch(b) -> StepInput:
                      b.swap_in, b.swap_out, b.copies)
 
 
+def prefill_step_input(ids, block_size: int, n_logits: int = 1) -> StepInput:
+    """A one-sequence prefill step over KV blocks 0.. (for checks run on a
+    fresh pool, before any request owns a block): logits of the last
+    ``n_logits`` positions."""
+    T = len(ids)
+    nb = (T + block_size - 1) // block_size
+    ints = np.concatenate([np.asarray(ids, dtype=np.int32), np.arange(T, dtype=np.int32),
+                           np.arange(T, dtype=np.int32), np.array([0, T], dtype=np.int32),
+                           np.array([T], dtype=np.int32), np.arange(nb, dtype=np.int32)])
+    empty = np.zeros((0, 2), dtype=np.int64)
+    return StepInput(1, 0, T, T, T, nb, ints,
+                     np.arange(T - n_logits, T, dtype=np.int32), empty, empty, empty)
+
+
 class ModelRunner:
     def __init__(self, model_cfg: ModelConfig, engine_cfg, device: torch.device,
                  tp: Optional[TPGroup] = None, max_model_len: Optional[int] = None):
@@ -271,6 +285,27 @@ class ModelRunner:
         with nvtx.range("forward"):
             h = self.model.forward(input_ids, meta, self.kv_cache)
             return self.model.compute_logits(h)
+
+    def release(self) -> None:
+        """Drop the graphs, the KV pools and the weights so their device
+        memory can be reused in the same process (bench arms run back to
+        back); the runner is unusable afterwards."""
+        if self.is_cuda:
+            torch.cuda.synchronize(self.device)
+        self.graphs = {}
+        self._gbuf = None
+        self.graph_pool = None
+        self.kv_cache = None
+        self.cpu_cache = None
+        self._decode_ws = None
+        self.model = None
+        close = getattr(self.tp, "close", None)
+        if close is not None:
+            close()
+        if self.is_cuda:
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
 
     # ----------------------------------------------------------- CUDA graphs
     def _graph_for(self, n: int) -> Optional[int]:

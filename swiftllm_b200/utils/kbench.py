@@ -178,161 +178,6 @@ def step_case(S, ctx, model="llama-2-7b", eager=False, once=False, iters=20):
             "kv_GB": round(kv / 1e9, 2), "frac_bw": round((w + kv) / ms / 1e9 / (pk["hbm_gbs"] / 1e3), 3)}
 
 
-def sk_sweep(T=256):
-    """Stream-K decode GEMM settings (features per unit, minimum k-iterations
-    per CTA) for the Llama-2-7B projections; plus the data-parallel kernel
-    (SWIFT_GEMM_STREAMK=0) and cuBLAS for comparison."""
-    import os
-    res = []
-    for N, K in [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008), (32000, 4096)]:
-        os.environ["SWIFT_GEMM_STREAMK"] = "0"
-        base = gemm_case(T, N, K)
-        os.environ["SWIFT_GEMM_STREAMK"] = "2"
-        best = None
-        for bn in (64, 128, 256):
-            for mp in (8, 32, 128):
-                os.environ["SWIFT_SK_MT"] = "1"
-                os.environ["SWIFT_SK_BN"] = str(bn)
-                os.environ["SWIFT_SK_MINPER"] = str(mp)
-                r = gemm_case(T, N, K, cublas=False)
-                r["mt"], r["minper"], r["bn"] = 1, mp, bn
-                print(json.dumps(r), flush=True)
-                if best is None or r["ms"] < best["ms"]:
-                    best = r
-        for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_GEMM_STREAMK", "SWIFT_SK_BN"):
-            os.environ.pop(k, None)
-        dflt = gemm_case(T, N, K, cublas=False)
-        out = {"N": N, "K": K, "T": T, "dp_ms": base["ms"], "cublas_ms": base["cublas_ms"],
-               "sk_default_ms": dflt["ms"], "sk_default_plan": dflt["plan"],
-               "sk_best_ms": best["ms"], "sk_best": [best["bn"], best["minper"]],
-               "sk_best_TB/s": best["TB/s"], "sk_best_frac_bw": best["frac_bw"]}
-        print(json.dumps(out), flush=True)
-        res.append(out)
-    return res
-
-
-def sk_probe(T=256):
-    """Load-only (probe 1) and MMA-only (probe 2) timings of the stream-K
-    kernel next to the full kernel (probe 0): which side bounds it."""
-    import os
-    res = []
-    for N, K in [(12288, 4096), (4096, 11008)]:
-        for mt in (1,):
-            for probe in (0, 2, 64, 66, 130, 194):
-                os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": "16",
-                                   "SWIFT_SK_PROBE": str(probe), "SWIFT_GEMM_STREAMK": "2"})
-                r = gemm_case(T, N, K, cublas=False)
-                r.update(mt=mt, probe=probe)
-                print(json.dumps(r), flush=True)
-                res.append(r)
-    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_SK_PROBE"):
-        os.environ.pop(k, None)
-    return res
-
-
-def sk_stamps(T=256, N=12288, K=4096, mt=1, minper=16, probe=0):
-    """Phase timing of one stream-K launch (SWIFT_SK_PROBE bit 4): per CTA, the
-    %globaltimer stamps relative to the earliest kernel start, as
-    percentiles over CTAs (microseconds)."""
-    import os
-    import numpy as np
-    os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": str(minper),
-                       "SWIFT_SK_PROBE": str(4 | probe), "SWIFT_GEMM_STREAMK": "2"})
-    C = cuda_ext()
-    x = torch.randn(T, K, device="cuda").bfloat16()
-    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
-    y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
-    flush = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
-    for _ in range(3):
-        C.gemm(y, x, w, None)
-    flush.sum()
-    torch.cuda.synchronize()
-    C.gemm_sk_stamps()
-    C.gemm(y, x, w, None)
-    torch.cuda.synchronize()
-    st = C.gemm_sk_stamps().numpy().astype(np.float64)
-    plan = C.gemm_plan(N, T, K)
-    g = int(plan[3])
-    st = st[:g]
-    t0 = st[:, 0].min()
-    names = ["start", "s0_ready", "s0_partial", "s0_done", "s1_ready", "s1_partial", "s1_done",
-             "s2_ready", "s2_partial", "s2_done"]
-    out = {"plan": plan, "probe": probe, "rot": os.environ.get("SWIFT_SK_ROT", "0")}
-    for k, nm in enumerate(names):
-        col = st[:, k]
-        col = col[col > 0]
-        if col.size:
-            rel = (col - t0) / 1e3
-            out[nm] = [round(float(np.percentile(rel, p)), 2) for p in (0, 50, 100)]
-    end = (st[:, 15] - t0) / 1e3
-    out["end"] = [round(float(np.percentile(end, p)), 2) for p in (0, 50, 100)]
-    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER", "SWIFT_SK_PROBE"):
-        os.environ.pop(k, None)
-    print(json.dumps(out), flush=True)
-    return out
-
-
-def pack_weight(w):
-    """[M, K] -> tile-packed [ceil(M/128), ceil(K/64), 128, 64], zero padded."""
-    M, K = w.shape
-    Mp, Kp = (M + 127) // 128 * 128, (K + 63) // 64 * 64
-    wp = torch.zeros(Mp, Kp, dtype=w.dtype, device=w.device)
-    wp[:M, :K] = w
-    return wp.view(Mp // 128, 128, Kp // 64, 64).permute(0, 2, 1, 3).contiguous()
-
-
-def pack_test(T=256):
-    """Row-major vs tile-packed weights in the stream-K kernel, with and
-    without an L2 flush between runs (is the weight stream DRAM-locality
-    bound?)."""
-    import os
-    C = cuda_ext()
-    res = []
-    for N, K in [(12288, 4096), (22016, 4096), (4096, 11008), (4096, 4096)]:
-        x = torch.randn(T, K, device="cuda").bfloat16()
-        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
-        wp = pack_weight(w)
-        y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
-        y2 = torch.empty_like(y)
-        for mt in (1, 2):
-            for mp in (8, 16):
-                os.environ.update({"SWIFT_SK_MT": str(mt), "SWIFT_SK_MINPER": str(mp),
-                                   "SWIFT_GEMM_STREAMK": "2"})
-                C.gemm(y, x, w, None)
-                C.gemm_packed(y2, x, wp, N, None)
-                torch.cuda.synchronize()
-                assert torch.equal(y, y2)
-                r = {"N": N, "K": K, "mt": mt, "minper": mp,
-                     "rowmajor_ms": round(_time(lambda: C.gemm(y, x, w, None)), 4),
-                     "packed_ms": round(_time(lambda: C.gemm_packed(y2, x, wp, N, None)), 4),
-                     "rowmajor_l2hot_ms": round(_time(lambda: C.gemm(y, x, w, None), flush=False), 4),
-                     "packed_l2hot_ms": round(_time(lambda: C.gemm_packed(y2, x, wp, N, None), flush=False), 4)}
-                print(json.dumps(r), flush=True)
-                res.append(r)
-    for k in ("SWIFT_SK_MT", "SWIFT_SK_MINPER"):
-        os.environ.pop(k, None)
-    return res
-
-
-def mixed_sweep():
-    """Mixed prefill + decode token counts: data-parallel plan vs stream-K."""
-    import os
-    res = []
-    for T in (300, 626, 1000, 1500):
-        for N, K in [(12288, 4096), (4096, 4096), (22016, 4096), (4096, 11008)]:
-            os.environ["SWIFT_GEMM_STREAMK"] = "0"
-            dp = gemm_case(T, N, K, cublas=True)
-            os.environ["SWIFT_GEMM_STREAMK"] = "2"
-            sk = gemm_case(T, N, K, cublas=False)
-            r = {"T": T, "N": N, "K": K, "dp_ms": dp["ms"], "sk_ms": sk["ms"],
-                 "cublas_ms": dp["cublas_ms"], "sk_plan": sk["plan"], "dp_plan": dp["plan"]}
-            print(json.dumps(r), flush=True)
-            res.append(r)
-    for k in ("SWIFT_GEMM_STREAMK",):
-        os.environ.pop(k, None)
-    return res
-
-
 def fp8_case(T, N, K):
     """E4M3 GEMM (per-row scales) vs the bf16 GEMM of the same shape; the fp8
     time includes the activation quantisation kernel."""
@@ -369,7 +214,7 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "sksweep", "skprobe", "skstamps", "packtest", "mixed", "fp8"])
+    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "fp8"])
     ap.add_argument("--model", default="llama-2-7b")
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
@@ -379,23 +224,12 @@ def main(argv=None):
     a = ap.parse_args(argv)
     if a.op == "sweep":
         res = sweep()
-    elif a.op == "skstamps":
-        shp = [int(v) for v in (a.shape or "256,12288,4096,1,16").split(",")]
-        res = sk_stamps(*shp)
     elif a.op == "fp8":
         res = [fp8_case(*[int(v) for v in c.split("x")]) for c in
                (a.shape or "256x12288x4096,256x22016x4096,256x4096x11008,8192x12288x4096").split(",")]
         for r in res:
             print(json.dumps(r), flush=True)
         res = None
-    elif a.op == "mixed":
-        res = mixed_sweep()
-    elif a.op == "packtest":
-        res = pack_test()
-    elif a.op == "skprobe":
-        res = sk_probe()
-    elif a.op == "sksweep":
-        res = sk_sweep(int(a.shape) if a.shape else 256)
     else:
         shp = [int(v) for v in a.shape.split(",")]
         if a.op == "gemm":

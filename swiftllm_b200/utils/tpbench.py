@@ -55,18 +55,6 @@ def main():
         for T in [int(v) for v in a.tokens.split(",")]:
             x = torch.randn(T, K, device=dev).bfloat16()
             t_fused = _time(lambda: tp.linear_reduce(x, w, fused=True))
-            variants = {}
-            for var in os.environ.get("SWIFT_TPBENCH_VARIANTS", "").split(";"):
-                if not var:
-                    continue
-                k_, v_ = var.split("=")
-                old = os.environ.get(k_)
-                os.environ[k_] = v_
-                variants[var] = round(_time(lambda: tp.linear_reduce(x, w, fused=True)), 4)
-                if old is None:
-                    os.environ.pop(k_)
-                else:
-                    os.environ[k_] = old
             t_unfused = _time(lambda: tp.linear_reduce(x, w, fused=False))
             t_gemm = _time(lambda: ops.linear(x, w, out=tp.reduce_buffer(T, a.hidden)))
             y = torch.empty(T, a.hidden, device=dev, dtype=torch.bfloat16)
@@ -79,7 +67,7 @@ def main():
                 print(json.dumps({"K": K, "T": T, "fused_ms": round(t_fused, 4),
                                   "unfused_ms": round(t_unfused, 4),
                                   "gemm_only_ms": round(t_gemm, 4),
-                                  "cublas_nccl_ms": round(t_nccl, 4), **variants}), flush=True)
+                                  "cublas_nccl_ms": round(t_nccl, 4)}), flush=True)
     st = tp.C.read_status(True)
     if rank == 0:
         print(json.dumps({"status": list(st)}), flush=True)

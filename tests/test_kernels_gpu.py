@@ -185,12 +185,17 @@ def test_gemm(C, T, N, K):
 @pytest.mark.parametrize("T,N,K", [(5, 640, 200), (100, 4096, 4096), (256, 12288, 4096),
                                    (64, 384, 11008), (200, 32000, 1024), (600, 1000, 640),
                                    (1000, 2048, 1024)])
-def test_gemm_streamk(C, monkeypatch, mt, minper, T, N, K):
+def test_gemm_streamk(C, mt, minper, T, N, K):
     # stream-K decode path: forced unit height and tiny per-CTA ranges so
     # tiles are split across many CTAs (partials + last-arriver fix-up)
-    monkeypatch.setenv("SWIFT_GEMM_STREAMK", "2")
-    monkeypatch.setenv("SWIFT_SK_MT", str(mt))
-    monkeypatch.setenv("SWIFT_SK_MINPER", str(minper))
+    C.gemm_streamk_config(2, mt, minper)
+    try:
+        _check_streamk(C, mt, T, N, K)
+    finally:
+        C.gemm_streamk_config(1, 1, 32)
+
+
+def _check_streamk(C, mt, T, N, K):
     plan = C.gemm_plan(N, T, K)
     assert plan[2] == mt
     x, w, b = bf(T, K, scale=0.5), bf(N, K, scale=0.05), bf(N)
