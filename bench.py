@@ -248,9 +248,13 @@ def tp_reference_logits(model: str, ekw: dict):
     si = prefill_step_input(ids, cfg.block_size, CHECK_ROWS)
     runner.allocate_kv(si.max_blocks + 1, 0)
     logits = runner.execute(si).float().cpu()
+    # the same single-GPU forward with our GEMMs: how far two correct bf16
+    # forwards of these weights differ (the tolerance of the TP check)
+    ops.set_gemm_backend("tcgen05")
+    alt = runner.execute(si).float().cpu()
     runner.release()
     ops.set_gemm_backend(ops.DEFAULT_GEMM_BACKEND)
-    return ids, logits
+    return ids, (logits, alt)
 
 
 def tp_logits_check(eng, ids, ref) -> dict:
@@ -261,14 +265,18 @@ def tp_logits_check(eng, ids, ref) -> dict:
     from swiftllm_b200.runtime.model_runner import prefill_step_input
     si = prefill_step_input(ids, eng.config.block_size, CHECK_ROWS)
     got = eng.executor.execute(si).float().cpu()
+    ref, alt = ref
     err = (got - ref).abs().max().item()
+    noise = (alt - ref).abs().max().item()
     scale = ref.abs().max().item()
     cos = torch.nn.functional.cosine_similarity(got, ref, dim=-1).min().item()
-    agree = (got.argmax(-1) == ref.argmax(-1)).float().mean().item()
-    return {"vs": "tp1 single-GPU forward, same weights", "rows": CHECK_ROWS,
+    cos_noise = torch.nn.functional.cosine_similarity(alt, ref, dim=-1).min().item()
+    return {"vs": "tp1 single-GPU forward (cuBLAS GEMMs), same weights", "rows": CHECK_ROWS,
             "max_abs_err": round(err, 4), "ref_max_abs": round(scale, 4),
-            "min_cosine": round(cos, 6), "argmax_agree": round(agree, 3),
-            "ok": bool(cos > 0.999 and err < 0.05 * max(scale, 1e-6))}
+            "min_cosine": round(cos, 6),
+            "tp1_tcgen05_vs_cublas": {"max_abs_err": round(noise, 4),
+                                      "min_cosine": round(cos_noise, 6)},
+            "ok": bool(err <= 2.0 * noise + 1e-3 * scale)}
 
 
 def run_arm(args, wl, arm: str, rank: int, check=None):

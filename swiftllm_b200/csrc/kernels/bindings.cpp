@@ -36,20 +36,17 @@ void gemm_streamk_config(int64_t mode, int64_t mt, int64_t min_per);
 void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x);
 int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
                   torch::Tensor wscale, c10::optional<torch::Tensor> bias);
-int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-                std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t s_max,
-                int64_t flag_off, torch::Tensor ctr);
-void tp_rs_finish(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
-                  int64_t s_max, int64_t T, int64_t H, int64_t flag_off, torch::Tensor gemm_epochs,
-                  torch::Tensor epochs, double timeout_s);
-void tp_rs_finish_norm(std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t out_off,
-                       int64_t res_off, torch::Tensor residual, torch::Tensor w, double eps,
-                       int64_t s_max, int64_t T, int64_t H, int64_t flag_off,
-                       torch::Tensor gemm_epochs, torch::Tensor epochs, double timeout_s);
 int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
                     c10::optional<torch::Tensor> bias);
-void tp_allreduce(torch::Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t in_off,
-                  int64_t red_off, torch::Tensor epochs, double timeout_s);
+int64_t tp_reduce_norm(std::vector<int64_t> bases, int64_t mc, int64_t rank, int64_t in_off,
+                       int64_t out_off, int64_t ctr_off, c10::optional<torch::Tensor> residual,
+                       c10::optional<torch::Tensor> w, double eps, int64_t T, int64_t H,
+                       torch::Tensor epochs, double timeout_s);
+int64_t tp_vocab_argmax(std::vector<int64_t> bases, int64_t mc, int64_t rank, torch::Tensor logits,
+                        int64_t v0, int64_t cand_off, int64_t ctr_off, torch::Tensor tokens,
+                        torch::Tensor lps, torch::Tensor epochs, double timeout_s);
+int64_t gemm2(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
+std::vector<int64_t> gemm2_plan_py(int64_t M, int64_t N, int64_t K);
 void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s);
 int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor offsets,
                      int64_t avg_rows);
@@ -80,13 +77,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_plan", &swift::gemm_plan);
   m.def("gemm_streamk_config", &swift::gemm_streamk_config);
   m.def("gemm_packed", &swift::gemm_packed);
-  m.def("gemm_rs", &swift::gemm_rs);
   m.def("gemm_e4m3", &swift::gemm_e4m3);
   m.def("quantize_e4m3", &swift::quantize_e4m3);
-  m.def("tp_rs_finish", &swift::tp_rs_finish);
-  m.def("tp_rs_finish_norm", &swift::tp_rs_finish_norm);
-  m.def("tp_allreduce", &swift::tp_allreduce);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
+  m.def("gemm2", &swift::gemm2);
+  m.def("gemm2_plan", &swift::gemm2_plan_py);
+  m.def("tp_reduce_norm", &swift::tp_reduce_norm);
+  m.def("tp_vocab_argmax", &swift::tp_vocab_argmax);
   m.def("gemm_grouped", &swift::gemm_grouped);
   m.def("moe_route", &swift::moe_route);
   m.def("moe_permute", &swift::moe_permute);

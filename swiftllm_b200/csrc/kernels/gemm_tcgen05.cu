@@ -859,6 +859,9 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
 }
 
 // ---------------------------------------------------------------- host side
+int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, const torch::Tensor& w,
+                     const __nv_bfloat16* bias);
+
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -1118,6 +1121,9 @@ static int64_t gemm_impl(__nv_bfloat16* y, int64_t ldy, torch::Tensor x, torch::
   const __nv_bfloat16* bp =
       bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
                        : nullptr;
+  // more than 256 tokens: the 2-SM kernel (gemm_2sm.cu), measured faster
+  // than this one-SM kernel at every such Llama projection shape on B200
+  if (T > 256 && sc.k == 0) return gemm2_launch(y, ldy, x, w, bp);
   if (gemm_streamk(y, x, w, bp, T, ldx, ldy, 0, 0, sc)) return 1;
   int bn, splits;
   plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);
@@ -1154,36 +1160,6 @@ int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<
   const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : w.size(0);
   return gemm_impl(reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), ldy, x, w,
                    bias, ScatterDesc{});
-}
-
-// Fused GEMM -> reduce-scatter (tensor parallelism): y = x . w^T is not
-// stored locally; each output row goes to the receive buffer of the rank
-// owning that token (see ScatterDesc). `ctr` (int32 [4], this rank) holds
-// the completion epoch and the CTA counter. Returns launches.
-int64_t gemm_rs(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
-                std::vector<int64_t> bases, int64_t rank, int64_t in_off, int64_t s_max,
-                int64_t flag_off, torch::Tensor ctr) {
-  const int k = static_cast<int>(bases.size());
-  TORCH_CHECK(k >= 2 && k <= 8, "gemm_rs: 2..8 ranks");
-  TORCH_CHECK(ctr.scalar_type() == at::kInt && ctr.numel() >= 4 && ctr.is_cuda());
-  TORCH_CHECK(in_off % 16 == 0 && flag_off % 4 == 0);
-  const int64_t K = x.size(-1), T = x.numel() / K, H = w.size(0);
-  TORCH_CHECK(H % 8 == 0, "gemm_rs: output width must be a multiple of 8");
-  TORCH_CHECK((T + k - 1) / k <= s_max, "gemm_rs: token shard exceeds the receive slots");
-  ScatterDesc sc{};
-  for (int r = 0; r < 8; ++r) sc.base[r] = r < k ? static_cast<uint64_t>(bases[r]) : 0;
-  sc.in_off = in_off;
-  sc.flag_off = flag_off;
-  sc.ctr = reinterpret_cast<uint32_t*>(ctr.data_ptr<int32_t>());
-  sc.k = k;
-  sc.rank = static_cast<int>(rank);
-  sc.s_max = static_cast<int>(s_max);
-  sc.T = static_cast<int>(T);
-  sc.H = static_cast<int>(H);
-  // every thread fences its own remote stores before the CTA publishes
-  sc.fence_all = 1;
-  if (T == 0) return 0;
-  return gemm_impl(nullptr, 0, x, w, bias, sc);
 }
 
 // Weights in tile-packed order: w_packed [ceil(M/128), ceil(K/64), 128, 64]

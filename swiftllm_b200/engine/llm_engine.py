@@ -253,6 +253,11 @@ class LLMEngine:
             return outs
         from ..runtime.model_runner import step_input_from_batch
         si = step_input_from_batch(b)
+        want_lp_rows = self._wants_logprobs(b) if b.num_sample_rows else False
+        if self.config.tensor_parallel_size > 1 and b.num_sample_rows and not b.any_penalty \
+                and not want_lp_rows:
+            temp = np.asarray(b.temperature)
+            si.greedy = bool(np.all((temp <= 0.0) | (np.asarray(b.top_k) == 1)))
         logits = self.executor.execute(si)
         if b.num_sample_rows == 0:
             self.last_step_tokens = 0
@@ -263,7 +268,7 @@ class LLMEngine:
             return outs
         with nvtx.range("sample"):
             toks, lps = self.sampler(logits, b, self._history)
-        want_lp = self._top_logprobs(logits, b, toks) if self._wants_logprobs(b) else None
+        want_lp = self._top_logprobs(logits, b, toks) if want_lp_rows else None
         res = self.scheduler.update(b, toks, lps, time.monotonic())
         self._gen_tokens += len(res.token)
         self._account(si, b, len(res.token))

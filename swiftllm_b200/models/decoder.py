@@ -14,9 +14,11 @@ Layout (one process per GPU, tensor parallel over ``tp.size`` ranks):
   w13    [2 I / tp, H]             gate rows then up rows (per rank)
   w2     [H, I / tp]               row-parallel -> reduction across ranks
   MoE    router [E, H] (replicated), w13 [E, 2 I / tp, H], w2 [E, H, I / tp]
-The residual stream is replicated on every rank; the reduction after each
-row-parallel GEMM is the fused GEMM + NVLink reduce (``tp.reduce``), or
-NCCL all-reduce in the baseline backend.
+Under the fused backend the residual stream is sharded by token rows and
+each row-parallel reduction is one kernel that also adds the residual,
+normalises and all-gathers (``_forward_seq_parallel``, ``tp.reduce_norm``);
+under the NCCL baseline the residual is replicated and each row-parallel
+output is all-reduced (``tp.reduce``).
 """
 
 from __future__ import annotations
@@ -74,11 +76,6 @@ class TPGroup:
         if self.size > 1 and self.rank != 0:
             b = None
         return self.reduce(ops.linear(x, w, b))
-
-    def linear_reduce_norm(self, x: torch.Tensor, w: torch.Tensor, norm_w: torch.Tensor,
-                           eps: float, residual: torch.Tensor):
-        """linear_reduce, then residual add + RMSNorm: (normed, residual)."""
-        return ops.rms_norm(self.linear_reduce(x, w), norm_w, eps, residual)
 
 
 def _shard(n: int, rank: int, size: int):
@@ -282,18 +279,6 @@ class DecoderModel:
             return self.tp.linear_reduce(a2, L.wo)
         return ops.linear(a2, L.wo)
 
-    def _attention_norm(self, i, L, x, meta, kv_cache, residual):
-        c = self.cfg
-        q = ops.qkv_rope_cache(ops.linear(x, L.wqkv), meta.positions, self.cos_sin, kv_cache, i,
-                               meta.slot_mapping, self.local_heads, self.local_kv_heads,
-                               c.head_dim, c.rotary_dim, L.bqkv)
-        a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
-        return self.tp.linear_reduce_norm(a.reshape(a.shape[0], -1), L.wo, L.ln2, c.rms_norm_eps,
-                                          residual)
-
-    def _mlp_hidden(self, L, x):
-        return ops.silu_and_mul(ops.linear(x, L.w13))
-
     def _reduce_slot(self, T: int):
         """Where a row-parallel GEMM should write its partial output: the
         fused TP backend hands out its NVLink-visible buffer (GEMM -> reduce
@@ -318,13 +303,50 @@ class DecoderModel:
             return self.tp.linear_reduce(h, L.w2)
         return ops.linear(h, L.w2)
 
+    def _seq_parallel(self) -> bool:
+        c = self.cfg
+        return (getattr(self.tp, "sequence_parallel", False) and self.device.type == "cuda"
+                and not c.parallel_block and c.norm_type != "layernorm")
+
+    def _forward_seq_parallel(self, input_ids, meta: AttnMeta, kv_cache) -> torch.Tensor:
+        """Tensor-parallel forward with a token-sharded residual: every
+        row-parallel GEMM stores its partial locally, and one kernel per
+        reduction sums this rank's token rows across ranks, adds the residual
+        shard, applies the next norm and all-gathers the normalised rows
+        (``tp.reduce_norm``). Returns the final-normed rows of logits_idx."""
+        c = self.cfg
+        T, H = int(input_ids.shape[0]), c.hidden_size
+        h = ops.embedding(input_ids, self.embed)  # residual (own token rows kept current)
+        x, _ = self._norm(h, self.layers[0].ln1, None)
+        n = len(self.layers)
+        for i, L in enumerate(self.layers):
+            q = ops.qkv_rope_cache(ops.linear(x, L.wqkv), meta.positions, self.cos_sin, kv_cache, i,
+                                   meta.slot_mapping, self.local_heads, self.local_kv_heads,
+                                   c.head_dim, c.rotary_dim, L.bqkv)
+            a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
+            ops.linear(a.reshape(T, -1), L.wo, out=self.tp.reduce_buffer(T, H))
+            x = self.tp.reduce_norm(T, h, L.ln2, c.rms_norm_eps)
+            if c.num_experts:
+                from ..parallel.moe import moe_forward
+                moe_forward(self, L, x)  # the combine stores into the reduce buffer
+            elif c.hidden_act.startswith("gelu"):
+                g = ops.gelu_tanh(ops.linear(x, L.w1, L.b1))
+                ops.linear(g, L.w2, L.b2 if self.tp.rank == 0 else None,
+                           out=self.tp.reduce_buffer(T, H))
+            else:
+                ops.linear(ops.silu_and_mul(ops.linear(x, L.w13)), L.w2,
+                           out=self.tp.reduce_buffer(T, H))
+            w_next = self.layers[i + 1].ln1 if i + 1 < n else self.norm_w
+            x = self.tp.reduce_norm(T, h, w_next, c.rms_norm_eps)
+        return x.index_select(0, meta.logits_idx)
+
     def forward(self, input_ids: torch.Tensor, meta: AttnMeta, kv_cache: torch.Tensor) -> torch.Tensor:
         """Returns final hidden states of the rows in ``meta.logits_idx``."""
         c = self.cfg
+        if self._seq_parallel():
+            return self._forward_seq_parallel(input_ids, meta, kv_cache)
         h = ops.embedding(input_ids, self.embed)
         residual = None
-        fuse_norm = (self.tp.size > 1 and not c.parallel_block and not c.num_experts
-                     and c.norm_type != "layernorm" and not c.hidden_act.startswith("gelu"))
         for i, L in enumerate(self.layers):
             if c.parallel_block:
                 x, _ = self._norm(h, L.ln1, L.ln1_b)
@@ -338,19 +360,6 @@ class DecoderModel:
                         s = s + L.b2
                 s = self.tp.reduce(s)
                 h = h + s
-                continue
-            if fuse_norm:
-                # the row-parallel reduction also does the residual add and
-                # the RMSNorm that follows it (one kernel under fused TP)
-                if i == 0:
-                    x, residual = self._norm(h, L.ln1, L.ln1_b, None)
-                x, residual = self._attention_norm(i, L, x, meta, kv_cache, residual)
-                if i + 1 < len(self.layers):
-                    nxt = self.layers[i + 1]
-                    x, residual = self.tp.linear_reduce_norm(
-                        self._mlp_hidden(L, x), L.w2, nxt.ln1, c.rms_norm_eps, residual)
-                else:
-                    h = self._mlp(L, x)
                 continue
             x, residual = self._norm(h, L.ln1, L.ln1_b, residual)
             a = self._attention(i, L, x, meta, kv_cache)
@@ -366,9 +375,14 @@ class DecoderModel:
         x, _ = self._norm(last_h, self.norm_w, self.norm_b, last_r)
         return x
 
-    def compute_logits(self, x: torch.Tensor) -> torch.Tensor:
-        """fp32 logits over the full vocabulary (gathered across ranks)."""
+    @property
+    def vocab_parallel(self) -> bool:
+        return self.vocab_end - self.vocab_start != self.cfg.vocab_size
+
+    def compute_logits(self, x: torch.Tensor, gather: bool = True) -> torch.Tensor:
+        """fp32 logits; under tensor parallelism this rank's vocabulary slice
+        [vocab_start, vocab_end), gathered over ranks when ``gather``."""
         logits = ops.linear(x, self.lm_head, self.lm_head_b).float()
-        if self.vocab_end - self.vocab_start != self.cfg.vocab_size:
+        if gather and self.vocab_parallel:
             logits = self.tp.gather_vocab(logits)
         return logits

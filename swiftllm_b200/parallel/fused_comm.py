@@ -1,33 +1,42 @@
-"""Fused tensor-parallel reduction over NVLink peer memory (the product
+"""Fused tensor-parallel communication over NVLink / NVSwitch (the product
 backend; NCCL is the baseline).
 
-The row-parallel GEMMs (o_proj, down_proj) write their partial sums straight
-into this rank's slot of a symmetric allocation (``reduce_buffer``); the
-reduction kernel (csrc/kernels/tp_allreduce.cu) then sums all ranks'
-partials with peer loads and per-block release/acquire flags, so no NCCL
-call sits on the per-layer path. The vocab-parallel logits gather stays on
-NCCL (one small call per step).
+Sequence-parallel layout of the decoder under this backend: the residual
+stream is sharded by token rows (rank j keeps rows [T*j/k, T*(j+1)/k)); the
+normalised activations that feed the next column-parallel GEMM are
+replicated. Each row-parallel GEMM (o_proj, down_proj, the MoE combine)
+stores its partial sum locally into this rank's ``in`` buffer of one
+symmetric allocation; then ONE kernel (csrc/kernels/tp_nvls.cu,
+``tp_reduce_norm``) per reduction
 
-Fused GEMM -> all-reduce (``linear_reduce`` for o_proj and down_proj, the
-default; SWIFTLLM_FUSED_GEMM_RS=0 turns it off): the GEMM epilogue stores each output row
-straight into the receive buffer of the rank that owns that token
-(reduce-scatter by NVLink stores, overlapped with the remaining GEMM tiles)
-and publishes a completion epoch; ``tp_rs_finish`` then sums each rank's own
-tokens and pushes them to every rank (all-gather by stores). Otherwise the
-GEMM writes this rank's partial into its symmetric slot and ``reduce`` runs
-the two-shot reduction kernel.
+  * reduce-scatters: each rank sums the k partials of its own token rows
+    with NVSwitch ``multimem.ld_reduce`` (fp32 accumulation in the switch)
+    or, without a multicast object, k NVLink peer loads;
+  * adds its residual shard and applies the next sub-block's RMSNorm;
+  * all-gathers: stores the normalised rows into every rank's ``out``
+    buffer with one ``multimem.st`` (or k peer stores).
+
+The next QKV / gate_up GEMM then reads ``out`` locally. Vocab-parallel
+greedy sampling (``vocab_greedy``) exchanges one (max, argmax, sum-exp)
+candidate per row and rank instead of gathering fp32 logits.
 
 Layout of the symmetric allocation (bytes):
-  [flags 64 KiB | in A | in B | red A | red B], each buffer (max_tokens + 8) x H
-  bf16. Flags: [phase][block][rank] u32 barrier slots at 0, the fused GEMM's
-  per-source completion epochs at 8 KiB. `in` doubles as the fused receive
-  buffer [src rank][ceil(max_tokens / k)][H].
+  [counters 32 KiB | in | out | out2 | cand]
+  counters: reduce_norm blocks at 0, plain all-reduce blocks at 1 KiB,
+  vocab rows at 4 KiB (up to 7168 rows); in / out / out2: (max_tokens + 8)
+  x H bf16; cand: k x max_rows float4.
+``SWIFTLLM_MULTIMEM=0`` forces the peer-load path (no multicast object).
+
+Parity: crates/swiftllm-core/src/execution/tensor_parallel.rs (all_reduce /
+all_gather / reduce_scatter :115-141, CommunicationBackend :55-63) and
+crates/swiftllm-models/src/layers/mod.rs (ColumnParallelLinear gather
+:113-118, RowParallelLinear reduce :145-149).
 """
 
 from __future__ import annotations
 
 import os
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -37,15 +46,17 @@ from .failures import CommTimeoutError
 
 log = get_logger(__name__)
 
-_FLAGS_BYTES = 64 << 10
-_GEMM_FLAG_OFF = 8 << 10
-FUSED_GEMM = os.environ.get("SWIFTLLM_FUSED_GEMM_RS", "1") == "1"
-# residual add + RMSNorm folded into the reduce's finish kernel
-FUSED_NORM = os.environ.get("SWIFTLLM_FUSED_NORM", "0") == "1"
+_CTR_BYTES = 32 << 10
+_CTR_NORM, _CTR_AR, _CTR_VOCAB = 0, 1 << 10, 4 << 10
+_RN_BLOCKS = 128          # kRnBlocks in tp_nvls.cu
+_MAX_ROWS = 7168          # vocab counters fit the counter region
 TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
+USE_MULTIMEM = os.environ.get("SWIFTLLM_MULTIMEM", "1") != "0"
 
 
 class FusedTP(NcclTP):
+    sequence_parallel = True
+
     def __init__(self, rank: int, size: int, device: torch.device, model_cfg,
                  max_tokens: int = 8192):
         super().__init__(rank, size)
@@ -57,104 +68,104 @@ class FusedTP(NcclTP):
         H = model_cfg.hidden_size
         self.H = H
         self.max_tokens = max_tokens
-        self.max_elems = max_tokens * H
-        self.s_max = (max_tokens + size - 1) // size
+        self.max_rows = min(_MAX_ROWS, max_tokens)
         self.buf_bytes = ((max_tokens + 8) * H * 2 + 255) // 256 * 256
-        total = _FLAGS_BYTES + 6 * self.buf_bytes
+        self.cand_bytes = (size * self.max_rows * 16 + 255) // 256 * 256
+        total = _CTR_BYTES + 3 * self.buf_bytes + self.cand_bytes
         self.symm = symm_mem.empty(total // 2, dtype=torch.bfloat16, device=device)
         self.symm.zero_()
         torch.cuda.synchronize(device)
         self.hdl = symm_mem.rendezvous(self.symm, dist.group.WORLD)
         self.bases = [int(p) for p in self.hdl.buffer_ptrs]
         assert len(self.bases) == size
-        self.epochs = torch.zeros(64, dtype=torch.int32, device=device)
-        self.gemm_ctr = torch.zeros(4, dtype=torch.int32, device=device)
-        self.gemm_epochs = torch.zeros(64, dtype=torch.int32, device=device)
-        self.call = 0
+        mc = 0
+        if USE_MULTIMEM:
+            try:
+                mc = int(self.hdl.multicast_ptr or 0)
+            except Exception as e:  # pragma: no cover - depends on the driver
+                log.warning("no NVLS multicast object (%s); using peer loads / stores", e)
+        self.mc = mc
+        self.in_off = _CTR_BYTES
+        self.out_off = _CTR_BYTES + self.buf_bytes
+        self.out2_off = _CTR_BYTES + 2 * self.buf_bytes
+        self.cand_off = _CTR_BYTES + 3 * self.buf_bytes
+        z = lambda n: torch.zeros(n, dtype=torch.int32, device=device)  # noqa: E731
+        self.ep_norm, self.ep_ar, self.ep_vocab = z(_RN_BLOCKS), z(_RN_BLOCKS), z(self.max_rows)
         dist.barrier()
-        log.info("fused TP comm ready: rank %d/%d, %.1f MiB symmetric", rank, size,
-                 total / 2**20)
+        log.info("fused TP comm ready: rank %d/%d, %.1f MiB symmetric, %s", rank, size,
+                 total / 2**20, "NVLS multimem" if mc else "peer loads/stores")
 
-    def _off(self, kind: str, parity: int) -> int:
-        base = _FLAGS_BYTES + {"in": 0, "red": 2, "res": 4}[kind] * self.buf_bytes
-        return base + parity * self.buf_bytes
+    # ------------------------------------------------------------ buffers
+    def _view(self, off: int, T: int, H: int) -> torch.Tensor:
+        return self.symm[off // 2:off // 2 + T * H].view(T, H)
 
     def reduce_buffer(self, T: int, H: int) -> Optional[torch.Tensor]:
-        """This rank's input slot for the next reduce: the producing GEMM
-        stores its partial output here."""
-        n = T * H
-        if n > self.max_elems:
+        """This rank's partial-sum buffer: the row-parallel GEMM stores its
+        output here (local stores)."""
+        if T > self.max_tokens or H != self.H:
             return None
-        off = self._off("in", self.call % 2) // 2
-        return self.symm[off:off + n].view(T, H)
+        return self._view(self.in_off, T, H)
+
+    def shard(self, T: int) -> Tuple[int, int]:
+        """Token rows [lo, hi) whose residual this rank keeps."""
+        return T * self.rank // self.size, T * (self.rank + 1) // self.size
+
+    # ------------------------------------------------------------ reductions
+    def reduce_norm(self, T: int, residual: torch.Tensor, w: Optional[torch.Tensor],
+                    eps: float) -> torch.Tensor:
+        """Sum of every rank's ``in`` rows, plus this rank's residual shard
+        (updated in place), RMS-normalised with ``w`` (None: no norm), all
+        rows gathered on every rank: returns the [T, H] normalised rows."""
+        from .. import ops
+        if T == 0:
+            return self._view(self.out_off, 0, self.H)
+        ops._count(self.C.tp_reduce_norm(self.bases, self.mc, self.rank, self.in_off, self.out_off,
+                                         _CTR_NORM, residual, w, float(eps), T, self.H,
+                                         self.ep_norm, TIMEOUT_S))
+        return self._view(self.out_off, T, self.H)
 
     def reduce(self, x: torch.Tensor) -> torch.Tensor:
-        n = x.numel()
-        if n > self.max_elems or n % 8:
+        """Plain all-reduce of a [T, H] tensor (sum over ranks)."""
+        T, H = x.shape[0], x.numel() // max(x.shape[0], 1)
+        if H != self.H or T > self.max_tokens:
             return super().reduce(x)
-        parity = self.call % 2
-        slot = self.reduce_buffer(x.shape[0], n // x.shape[0])
+        if T == 0:
+            return x
+        slot = self.reduce_buffer(T, H)
         if x.data_ptr() != slot.data_ptr():
-            slot.copy_(x.view_as(slot))
-        out = torch.empty_like(x)
-        self.C.tp_allreduce(out, self.bases, self.rank, self._off("in", parity),
-                            self._off("red", parity), self.epochs, TIMEOUT_S)
+            slot.copy_(x.view(T, H))
         from .. import ops
-        ops._count()
-        self.call += 1
-        return out
+        ops._count(self.C.tp_reduce_norm(self.bases, self.mc, self.rank, self.in_off, self.out2_off,
+                                         _CTR_AR, None, None, 0.0, T, H, self.ep_ar, TIMEOUT_S))
+        return self._view(self.out2_off, T, H).view_as(x)
 
-    def linear_reduce(self, x: torch.Tensor, w: torch.Tensor,
-                      b: Optional[torch.Tensor] = None, fused: Optional[bool] = None) -> torch.Tensor:
-        """Row-parallel linear + sum over ranks: either one fused GEMM ->
-        reduce-scatter kernel plus one reduce + all-gather kernel, or the GEMM
-        into this rank's slot plus the two-shot reduction."""
+    def linear_reduce(self, x: torch.Tensor, w, b: Optional[torch.Tensor] = None) -> torch.Tensor:
         from .. import ops
-        T, H = x.shape[0], w.shape[0]
         if self.rank != 0:
             b = None
-        fused = FUSED_GEMM if fused is None else fused
-        if (not fused or not isinstance(w, torch.Tensor) or x.shape[-1] % 8 or T == 0
-                or T > self.max_tokens or H != self.H
-                or ops.gemm_backend() != "tcgen05"):
-            return self.reduce(ops.linear(x, w, b, out=self.reduce_buffer(T, H)))
-        parity = self.call % 2
-        in_off, red_off = self._off("in", parity), self._off("red", parity)
-        n = self.C.gemm_rs(x, w, b, self.bases, self.rank, in_off, self.s_max, _GEMM_FLAG_OFF,
-                           self.gemm_ctr)
-        self.C.tp_rs_finish(self.bases, self.rank, in_off, red_off, self.s_max, T, H,
-                            _GEMM_FLAG_OFF, self.gemm_epochs, self.epochs, TIMEOUT_S)
-        ops._count(n + 1)
-        self.call += 1
-        return self.symm[red_off // 2:red_off // 2 + T * H].view(T, H)
+        T = x.shape[0]
+        return self.reduce(ops.linear(x, w, b, out=self.reduce_buffer(T, w.shape[0])))
 
-    def linear_reduce_norm(self, x: torch.Tensor, w: torch.Tensor, norm_w: torch.Tensor,
-                           eps: float, residual: torch.Tensor):
-        """Row-parallel linear, cross-rank sum, residual add and RMSNorm:
-        returns (normed, new residual) like ``ops.rms_norm(out, norm_w, eps,
-        residual)``. Fused path: the GEMM -> reduce-scatter kernel, then one
-        kernel that reduces each rank's own tokens, adds the residual,
-        normalises and all-gathers both rows."""
+    # ------------------------------------------------------------ sampling
+    def vocab_greedy(self, logits: torch.Tensor, v0: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Greedy tokens and their log-probabilities over the full vocabulary
+        from this rank's fp32 logits slice [rows, V/k] starting at ``v0``;
+        every rank gets the same result."""
         from .. import ops
-        T, H = x.shape[0], w.shape[0]
-        if (not (FUSED_GEMM and FUSED_NORM) or not isinstance(w, torch.Tensor) or x.shape[-1] % 8
-                or T == 0 or T > self.max_tokens or H != self.H or ops.gemm_backend() != "tcgen05"
-                or not residual.is_contiguous()):
-            return ops.rms_norm(self.linear_reduce(x, w), norm_w, eps, residual)
-        parity = self.call % 2
-        in_off, out_off, res_off = (self._off("in", parity), self._off("red", parity),
-                                    self._off("res", parity))
-        n = self.C.gemm_rs(x, w, None, self.bases, self.rank, in_off, self.s_max, _GEMM_FLAG_OFF,
-                           self.gemm_ctr)
-        self.C.tp_rs_finish_norm(self.bases, self.rank, in_off, out_off, res_off, residual, norm_w,
-                                 float(eps), self.s_max, T, H, _GEMM_FLAG_OFF, self.gemm_epochs,
-                                 self.epochs, TIMEOUT_S)
-        ops._count(n + 1)
-        self.call += 1
-        normed = self.symm[out_off // 2:out_off // 2 + T * H].view(T, H)
-        res = self.symm[res_off // 2:res_off // 2 + T * H].view(T, H)
-        return normed, res
+        rows = logits.shape[0]
+        if rows > self.max_rows:
+            full = self.gather_vocab(logits)
+            lp = torch.log_softmax(full, dim=-1)
+            tok = full.argmax(-1)
+            return tok.int(), lp.gather(1, tok.view(-1, 1)).view(-1)
+        tokens = torch.empty(rows, dtype=torch.int32, device=logits.device)
+        lps = torch.empty(rows, dtype=torch.float32, device=logits.device)
+        ops._count(self.C.tp_vocab_argmax(self.bases, self.mc, self.rank, logits.contiguous(), v0,
+                                          self.cand_off, _CTR_VOCAB, tokens, lps, self.ep_vocab,
+                                          TIMEOUT_S))
+        return tokens, lps
 
+    # ------------------------------------------------------------ lifecycle
     def close(self) -> None:
         """Release the symmetric allocation and its rendezvous handle (every
         rank calls this between steps, then a barrier, before the process
@@ -165,7 +176,7 @@ class FusedTP(NcclTP):
         self.hdl = None
         self.bases = []
         self.symm = None
-        self.epochs = self.gemm_ctr = self.gemm_epochs = None
+        self.ep_norm = self.ep_ar = self.ep_vocab = None
 
     def check(self) -> None:
         st = self.C.read_status(True)

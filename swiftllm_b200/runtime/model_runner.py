@@ -52,6 +52,15 @@ class StepInput:
     swap_in: np.ndarray       # [n, 2] (cpu, gpu)
     swap_out: np.ndarray      # [n, 2] (gpu, cpu)
     copies: np.ndarray        # [n, 2] (src, dst)
+    greedy: bool = False      # every sampled row is greedy, no logprobs / penalties
+
+
+@dataclass
+class GreedyResult:
+    """Device tensors [len(logits_idx)]: argmax token over the full
+    vocabulary and its log-probability (vocab-parallel greedy sampling)."""
+    tokens: torch.Tensor
+    lps: torch.Tensor
 
 
 def step_input_from_batch(b) -> StepInput:
@@ -284,7 +293,18 @@ class ModelRunner:
         input_ids, meta = self._meta_from(si, ints, lidx)
         with nvtx.range("forward"):
             h = self.model.forward(input_ids, meta, self.kv_cache)
-            return self.model.compute_logits(h)
+            return self._finish_logits(self.model.compute_logits(h, gather=False), si)
+
+    def _finish_logits(self, local: torch.Tensor, si: StepInput):
+        """Full-vocabulary fp32 logits, or, for an all-greedy step under
+        vocab-parallel TP with the fused backend, the merged greedy result
+        (no logits gather). Every rank calls this with the same ``si``."""
+        if not self.model.vocab_parallel:
+            return local
+        if si.greedy and hasattr(self.tp, "vocab_greedy"):
+            tok, lp = self.tp.vocab_greedy(local, self.model.vocab_start)
+            return GreedyResult(tok, lp)
+        return self.tp.gather_vocab(local)
 
     def release(self) -> None:
         """Drop the graphs, the KV pools and the weights so their device
@@ -351,13 +371,13 @@ class ModelRunner:
             with torch.cuda.stream(s):
                 for _ in range(2):
                     h = self.model.forward(buf["ids"][:b], meta, self.kv_cache)
-                    self.model.compute_logits(h)
+                    self.model.compute_logits(h, gather=False)
             torch.cuda.current_stream(dev).wait_stream(s)
             g = torch.cuda.CUDAGraph()
             n0 = ops.LAUNCHES[0]
             with torch.cuda.graph(g, pool=self.graph_pool):
                 h = self.model.forward(buf["ids"][:b], meta, self.kv_cache)
-                out = self.model.compute_logits(h)
+                out = self.model.compute_logits(h, gather=False)
             self.graphs[b] = (g, {"out": out, "launches": ops.LAUNCHES[0] - n0})
             ops.LAUNCHES[0] = n0
         torch.cuda.synchronize(dev)
@@ -382,4 +402,4 @@ class ModelRunner:
         g.replay()
         ops.LAUNCHES[0] += io["launches"]
         self.stats["graph_steps"] += 1
-        return io["out"][:n]
+        return self._finish_logits(io["out"][:n], si)

@@ -92,6 +92,9 @@ class BatchSampler:
         if n == 0:
             return np.zeros(0, np.int32), np.zeros(0, np.float32)
         lidx = np.asarray(b.sample_logit_idx, dtype=np.int32)
+        if hasattr(logits, "tokens"):  # vocab-parallel greedy result (all rows greedy)
+            both = torch.stack([logits.tokens.view(torch.float32), logits.lps]).cpu().numpy()
+            return both[0].view(np.int32)[lidx].copy(), both[1][lidx].copy()
         if b.any_penalty and history is not None:
             rows_logits = self._penalize(logits, b, lidx, history)
             lidx = np.arange(n, dtype=np.int32)

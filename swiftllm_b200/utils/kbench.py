@@ -55,14 +55,15 @@ def _time(fn, iters=20, flush=True):
     return ts[len(ts) // 2]
 
 
-def gemm_case(T, N, K, once=False, cublas=True):
+def gemm_case(T, N, K, once=False, cublas=True, kernel="gemm"):
+    """kernel: "gemm" (the ops.linear dispatch) or "gemm2" (the 2-SM kernel)."""
     C = cuda_ext()
     x = torch.randn(T, K, device="cuda").bfloat16()
     w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
     y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
     if once:
         for _ in range(4):
-            C.gemm(y, x, w, None)
+            getattr(C, kernel)(y, x, w, None)
         torch.cuda.synchronize()
         return {}
     pk = measured_peaks()
@@ -73,6 +74,8 @@ def gemm_case(T, N, K, once=False, cublas=True):
          "TB/s": round(byts / ms / 1e9, 2), "TFLOP/s": round(fl / ms / 1e9, 1),
          "frac_bw": round(byts / ms / 1e9 / (pk["hbm_gbs"] / 1e3), 3),
          "frac_flops": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
+    r["gemm2_ms"] = round(_time(lambda: C.gemm2(y, x, w, None)), 4)
+    r["gemm2_plan"] = C.gemm2_plan(N, T, K)
     if cublas:
         r["cublas_ms"] = round(_time(lambda: torch.matmul(x, w.t())), 4)
     return r

@@ -1,6 +1,10 @@
-"""Tensor-parallel row-parallel linear + sum: the fused GEMM -> reduce-scatter
-path against GEMM + the separate peer-memory reduction and against cuBLAS +
-NCCL, timed with CUDA events (median of 20, max over ranks).
+"""Tensor-parallel row-parallel linear + cross-rank sum + residual add +
+RMSNorm, the unit that closes every attention and MLP block: our GEMM into
+the symmetric buffer plus the one-kernel NVLS / peer reduction
+(``tp.reduce_norm``) against cuBLAS + NCCL all-reduce + the fused add-norm
+kernel. CUDA events, median of 20, max over ranks. Also reports the
+reduction alone and its fraction of the NVLink roofline: bytes each GPU must
+move per direction, (k-1)/k * T * H * 2, at the measured 770 GB/s.
 
   python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \\
       -m swiftllm_b200.utils.tpbench [--hidden 4096] [--inner 2048,5504] [--tokens 256,626]
@@ -14,6 +18,8 @@ import os
 
 import torch
 import torch.distributed as dist
+
+LINK_GBS = 770.0  # measured NVLink peer copy per direction on this pool's B200s
 
 
 def _time(fn, iters=20):
@@ -39,7 +45,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--hidden", type=int, default=4096)
     ap.add_argument("--inner", default="2048,5504")
-    ap.add_argument("--tokens", default="1,64,256,626,2048")
+    ap.add_argument("--tokens", default="1,64,256,832,2048,8192")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", rank)))
@@ -49,28 +55,42 @@ def main():
     init_distributed(rank, world, "nccl")
     cfg = ModelConfig(hidden_size=a.hidden)
     dev = torch.device("cuda", torch.cuda.current_device())
+    H = a.hidden
     tp = build_tp_group(rank, world, dev, "fused", cfg, 8192)
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     for K in [int(v) for v in a.inner.split(",")]:
-        w = (torch.randn(a.hidden, K, device=dev) * 0.02).bfloat16()
+        w = (torch.randn(H, K, device=dev) * 0.02).bfloat16()
         for T in [int(v) for v in a.tokens.split(",")]:
             x = torch.randn(T, K, device=dev).bfloat16()
-            t_fused = _time(lambda: tp.linear_reduce(x, w, fused=True))
-            t_unfused = _time(lambda: tp.linear_reduce(x, w, fused=False))
-            t_gemm = _time(lambda: ops.linear(x, w, out=tp.reduce_buffer(T, a.hidden)))
-            y = torch.empty(T, a.hidden, device=dev, dtype=torch.bfloat16)
+            res = torch.randn(T, H, device=dev).bfloat16()
+
+            def ours():
+                ops.linear(x, w, out=tp.reduce_buffer(T, H))
+                tp.reduce_norm(T, res, nw, 1e-5)
+            t_ours = _time(ours)
+            t_comm = _time(lambda: tp.reduce_norm(T, res, nw, 1e-5))
+            t_gemm = _time(lambda: ops.linear(x, w, out=tp.reduce_buffer(T, H)))
+            y = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
 
             def nccl():
                 torch.matmul(x, w.t(), out=y)
                 dist.all_reduce(y)
+                ops.rms_norm(y, nw, 1e-5, res)
             t_nccl = _time(nccl)
+            t_cublas = _time(lambda: torch.matmul(x, w.t(), out=y))
+            link_s = (world - 1) / world * T * H * 2 / (LINK_GBS * 1e9)
             if rank == 0:
-                print(json.dumps({"K": K, "T": T, "fused_ms": round(t_fused, 4),
-                                  "unfused_ms": round(t_unfused, 4),
-                                  "gemm_only_ms": round(t_gemm, 4),
-                                  "cublas_nccl_ms": round(t_nccl, 4)}), flush=True)
+                print(json.dumps({"K": K, "T": T, "ours_ms": round(t_ours, 4),
+                                  "reduce_norm_ms": round(t_comm, 4),
+                                  "gemm_ms": round(t_gemm, 4),
+                                  "cublas_nccl_norm_ms": round(t_nccl, 4),
+                                  "cublas_ms": round(t_cublas, 4),
+                                  "reduce_link_roofline_frac": round(link_s * 1e3 / t_comm, 3),
+                                  "multimem": bool(tp.mc)}), flush=True)
     st = tp.C.read_status(True)
     if rank == 0:
         print(json.dumps({"status": list(st)}), flush=True)
+    tp.close()
     dist.barrier()
     dist.destroy_process_group()
 

@@ -43,41 +43,50 @@ def main():
     cfg = load_config(name)
     tp = build_tp_group(rank, world, dev, "fused" if backend == "fused" else "nccl", cfg, 512)
     if backend == "fused":
-        # raw reduction check: sum of per-rank partials
         g = torch.Generator(device=dev).manual_seed(123 + rank)
-        for T in (1, 7, 256):
-            x = torch.randn(T, cfg.hidden_size, device=dev, generator=g).to(dtype)
+        H = cfg.hidden_size
+        for T in (1, 7, 256, 300):
+            # plain all-reduce: sum of per-rank partials
+            x = torch.randn(T, H, device=dev, generator=g).to(dtype)
             parts = [torch.empty_like(x) for _ in range(world)]
             dist.all_gather(parts, x)
             ref = torch.stack([p.float() for p in parts]).sum(0)
             got = tp.reduce(x.clone())
             torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=3e-2)
-        # fused GEMM -> reduce-scatter -> all-gather: sum over ranks of x_r . w_r^T
-        H = cfg.hidden_size
-        for T in (1, 7, 100, 256, 300, 7):
-            x = torch.randn(T, 64, device=dev, generator=g).to(dtype)
+            # GEMM partial into the reduce buffer, then reduce + residual
+            # shard + RMSNorm + all-gather in one kernel
+            xa = torch.randn(T, 64, device=dev, generator=g).to(dtype)
             w = (torch.randn(H, 64, device=dev, generator=g) * 0.1).to(dtype)
-            xs = [torch.empty_like(x) for _ in range(world)]
+            xs = [torch.empty_like(xa) for _ in range(world)]
             ws = [torch.empty_like(w) for _ in range(world)]
-            dist.all_gather(xs, x)
+            dist.all_gather(xs, xa)
             dist.all_gather(ws, w)
             ref = sum(a.float() @ b.float().t() for a, b in zip(xs, ws))
-            for fused in (True, False):
-                got = tp.linear_reduce(x, w, fused=fused)
-                torch.testing.assert_close(got.float(), ref, rtol=2e-2, atol=3e-2)
-            # + residual add + RMSNorm in the finish kernel
             res = torch.randn(T, H, device=dev, generator=g).to(dtype)
             dist.broadcast(res, 0)
             nw = (torch.rand(H, device=dev, generator=g) + 0.5).to(dtype)
             dist.broadcast(nw, 0)
             r_ref = (ref.to(dtype).float() + res.float()).to(dtype).float()
             n_ref = r_ref * torch.rsqrt(r_ref.pow(2).mean(-1, keepdim=True) + 1e-5) * nw.float()
-            import swiftllm_b200.parallel.fused_comm as fc
-            for on in (False, True):  # ends on: the model check below runs fused
-                fc.FUSED_NORM = on
-                got_n, got_r = tp.linear_reduce_norm(x, w, nw, 1e-5, res.clone())
-                torch.testing.assert_close(got_r.float(), r_ref, rtol=2e-2, atol=3e-2)
-                torch.testing.assert_close(got_n.float(), n_ref, rtol=3e-2, atol=3e-2)
+            from swiftllm_b200 import ops
+            ops.linear(xa, w, out=tp.reduce_buffer(T, H))
+            res_local = res.clone()
+            got_n = tp.reduce_norm(T, res_local, nw, 1e-5)
+            lo, hi = tp.shard(T)
+            torch.testing.assert_close(got_n.float(), n_ref, rtol=3e-2, atol=3e-2)
+            torch.testing.assert_close(res_local[lo:hi].float(), r_ref[lo:hi], rtol=2e-2, atol=3e-2)
+            # vocab-parallel greedy: argmax and log-prob over the full vocabulary
+            V = 1000
+            lg = torch.randn(T, V, device=dev, generator=g)
+            lg[0, 3 * rank + 1] = 50.0  # tie across ranks: the lowest index must win
+            lgs = [torch.empty_like(lg) for _ in range(world)]
+            dist.all_gather(lgs, lg)
+            full = torch.cat(lgs, dim=-1)
+            tok, lp = tp.vocab_greedy(lg, rank * V)
+            want = full.argmax(-1)
+            assert torch.equal(tok.long(), want), (tok[:4], want[:4])
+            ref_lp = torch.log_softmax(full, -1).gather(1, want.view(-1, 1)).view(-1)
+            torch.testing.assert_close(lp, ref_lp, rtol=1e-3, atol=1e-3)
         st = tp.C.read_status(True)
         assert st[0] == 0, st
     m = DecoderModel(cfg, dtype, dev, tp)
