@@ -256,6 +256,8 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3)
 template <int D>
 __global__ void decode_combine_kernel(__nv_bfloat16* __restrict__ out, const float* __restrict__ ws,
                                       int rows, int Hq, int splits) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   const int row = blockIdx.x, h = blockIdx.y;
   const int64_t base = (int64_t(row) * Hq + h) * splits;
   const float* ml = ws + int64_t(rows) * Hq * splits * D;
@@ -336,11 +338,13 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
     const int Hq = static_cast<int>(q.size(1));
     auto* op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
     if (D == 128)
-      decode_combine_kernel<128><<<dim3(rows, Hq), 128, 0, cur_stream()>>>(
-          op, ws.data_ptr<float>(), static_cast<int>(rows), Hq, static_cast<int>(splits));
+      launch_pdl(decode_combine_kernel<128>, dim3(rows, Hq), dim3(128), 0, cur_stream(), op,
+                 static_cast<const float*>(ws.data_ptr<float>()), static_cast<int>(rows), Hq,
+                 static_cast<int>(splits));
     else
-      decode_combine_kernel<64><<<dim3(rows, Hq), 128, 0, cur_stream()>>>(
-          op, ws.data_ptr<float>(), static_cast<int>(rows), Hq, static_cast<int>(splits));
+      launch_pdl(decode_combine_kernel<64>, dim3(rows, Hq), dim3(128), 0, cur_stream(), op,
+                 static_cast<const float*>(ws.data_ptr<float>()), static_cast<int>(rows), Hq,
+                 static_cast<int>(splits));
     SWIFT_CHECK_LAUNCH();
     return 2;
   }
@@ -371,26 +375,37 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
 #include "swift_noalloc.h"
 
 static __device__ __align__(256) float g_noalloc_scratch[SWIFT_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+// Status word of the allocation-free calls ([code, site], the same codes as
+// the library's own status word): a kernel that gives up a bounded wait
+// records it here; swift_noalloc_status() reads it back.
+static __device__ int g_noalloc_status[2];
 
 namespace swift {
 namespace {
 
 constexpr int kNoallocMaxDevices = 64;
 float* g_noalloc_ptr[kNoallocMaxDevices] = {nullptr};
+int* g_noalloc_status_ptr[kNoallocMaxDevices] = {nullptr};
 
-// Once per device, with that device current: the device address of the
-// scratch array (host code must not use the array's name as a pointer).
-int noalloc_setup(float** scratch) {
+// Once per device, with that device current: the device addresses of the
+// scratch array and the status word (host code must not use the arrays'
+// names as pointers).
+int noalloc_setup(float** scratch, int** status) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
   if (dev < 0 || dev >= kNoallocMaxDevices) return SWIFT_NOALLOC_ERR_CUDA;
   if (!g_noalloc_ptr[dev]) {
     void* p = nullptr;
+    void* ps = nullptr;
     if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
       return SWIFT_NOALLOC_ERR_CUDA;
+    if (cudaGetSymbolAddress(&ps, g_noalloc_status) != cudaSuccess || ps == nullptr)
+      return SWIFT_NOALLOC_ERR_CUDA;
+    g_noalloc_status_ptr[dev] = static_cast<int*>(ps);
     g_noalloc_ptr[dev] = static_cast<float*>(p);
   }
   *scratch = g_noalloc_ptr[dev];
+  *status = g_noalloc_status_ptr[dev];
   return SWIFT_NOALLOC_OK;
 }
 
@@ -398,7 +413,7 @@ template <int D, int BS>
 int noalloc_decode(void* out, const void* q, const void* kv, int64_t blk_stride, int64_t layer_off,
                    int64_t kv_stride, const int32_t* bt, int64_t bt_stride,
                    const int32_t* seq_lens, int rows, int Hq, int Hkv, int splits, float scale,
-                   int window, float* scratch, cudaStream_t stream) {
+                   int window, float* scratch, int* status, cudaStream_t stream) {
   using C = DecodeCfg<D, BS>;
   auto kern = paged_decode_kernel<D, BS>;
   static bool attr_set[kNoallocMaxDevices] = {false};
@@ -414,7 +429,7 @@ int noalloc_decode(void* out, const void* q, const void* kv, int64_t blk_stride,
   kern<<<grid, kDecWarps * 32, C::smem_for(Hq / Hkv), stream>>>(
       static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
       static_cast<const __nv_bfloat16*>(kv), blk_stride, layer_off, kv_stride, bt, bt_stride,
-      seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, nullptr);
+      seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, status);
   if (cudaGetLastError() != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
   if (splits > 1) {
     decode_combine_kernel<D><<<dim3(rows, Hq), 128, 0, stream>>>(
@@ -436,17 +451,30 @@ extern "C" __attribute__((visibility("default"))) int swift_paged_decode_noalloc
   if (!out || !q || !kv || !bt || !seq_lens || rows <= 0 || Hq <= 0 || Hkv <= 0 || splits <= 0)
     return SWIFT_NOALLOC_ERR_ARGS;
   if (Hq % Hkv != 0 || Hq / Hkv > kMaxGroup) return SWIFT_NOALLOC_ERR_UNSUPPORTED;
+  const bool shape_ok = (head_dim == 128 && (block_size == 8 || block_size == 16 || block_size == 32)) ||
+                        (head_dim == 64 && (block_size == 16 || block_size == 32)) ||
+                        ((head_dim == 80 || head_dim == 96) && block_size == 16);
+  if (!shape_ok) return SWIFT_NOALLOC_ERR_UNSUPPORTED;
+  // the kernel moves 16-byte pieces of q, out and every KV page (bulk
+  // copies): the pointers must be 16-byte aligned and the element offsets
+  // multiples of 8 bf16
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(out) || !al16(q) || !al16(kv) || blk_stride % 8 || layer_off % 8 || kv_stride % 8 ||
+      blk_stride <= 0 || kv_stride <= 0 || layer_off < 0 || bt_stride <= 0)
+    return SWIFT_NOALLOC_ERR_ARGS;
   const uint64_t need = splits > 1
       ? static_cast<uint64_t>(rows) * Hq * splits * (static_cast<uint64_t>(head_dim) + 2) * sizeof(float)
       : 0;
   if (need > SWIFT_NOALLOC_SCRATCH_BYTES) return SWIFT_NOALLOC_ERR_TOO_LARGE;
   float* scratch = nullptr;
-  int st = noalloc_setup(&scratch);
+  int* status = nullptr;
+  int st = noalloc_setup(&scratch, &status);
   if (st != SWIFT_NOALLOC_OK) return st;
 #define NOALLOC_CASE(d, bs)                                                                     \
   if (head_dim == d && block_size == bs)                                                        \
     return noalloc_decode<d, bs>(out, q, kv, blk_stride, layer_off, kv_stride, bt, bt_stride,   \
-                                 seq_lens, rows, Hq, Hkv, splits, scale, window, scratch, stream);
+                                 seq_lens, rows, Hq, Hkv, splits, scale, window, scratch, status, \
+                                 stream);
   NOALLOC_CASE(128, 16)
   NOALLOC_CASE(128, 32)
   NOALLOC_CASE(128, 8)
@@ -456,4 +484,25 @@ extern "C" __attribute__((visibility("default"))) int swift_paged_decode_noalloc
   NOALLOC_CASE(96, 16)
 #undef NOALLOC_CASE
   return SWIFT_NOALLOC_ERR_UNSUPPORTED;
+}
+
+// Reads (and with clear != 0 resets) the status word of the allocation-free
+// calls on the current device. Synchronous: it waits for the device.
+extern "C" __attribute__((visibility("default"))) int swift_noalloc_status(int* code, int* site,
+                                                                           int clear) {
+  using namespace swift;
+  if (!code || !site) return SWIFT_NOALLOC_ERR_ARGS;
+  float* scratch = nullptr;
+  int* status = nullptr;
+  int st = noalloc_setup(&scratch, &status);
+  if (st != SWIFT_NOALLOC_OK) return st;
+  int h[2] = {0, 0};
+  if (cudaMemcpyFromSymbol(h, g_noalloc_status, sizeof(h)) != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  *code = h[0];
+  *site = h[1];
+  if (clear) {
+    const int z[2] = {0, 0};
+    if (cudaMemcpyToSymbol(g_noalloc_status, z, sizeof(z)) != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
+  }
+  return SWIFT_NOALLOC_OK;
 }

@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(kTcWarps * 32, 3)
                            int64_t bt_stride, const int32_t* __restrict__ seq_lens, int Hq, int Hkv,
                            int splits, float scale_log2, int window, float* __restrict__ ws,
                            int* status) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   using C = TcCfg<D>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring =
@@ -290,7 +292,7 @@ void launch_tc(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t lay
   const int rows_per_blk = L * 2 * Hkv * kTcBS;
   const int layer_row_off = static_cast<int>(layer) * 2 * Hkv * kTcBS;
   dim3 grid(rows, Hkv, splits);
-  kern<<<grid, kTcWarps * 32, C::smem_for(Hq / Hkv), cur_stream()>>>(
+  launch_pdl(kern, dim3(grid), dim3(kTcWarps * 32), C::smem_for(Hq / Hkv), cur_stream(), 
       tm, reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr<at::BFloat16>()), rows_per_blk,
       layer_row_off, bt.data_ptr<int32_t>(), bt.stride(0), seq_lens.data_ptr<int32_t>(), Hq, Hkv,

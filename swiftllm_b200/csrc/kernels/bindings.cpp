@@ -45,7 +45,8 @@ int64_t tp_reduce_norm(std::vector<int64_t> bases, int64_t mc, int64_t rank, int
 int64_t tp_vocab_argmax(std::vector<int64_t> bases, int64_t mc, int64_t rank, torch::Tensor logits,
                         int64_t v0, int64_t cand_off, int64_t ctr_off, torch::Tensor tokens,
                         torch::Tensor lps, torch::Tensor epochs, double timeout_s);
-int64_t gemm2(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
+int64_t gemm2(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
+              int64_t plan, int64_t bn, int64_t splits);
 std::vector<int64_t> gemm2_plan_py(int64_t M, int64_t N, int64_t K);
 void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s);
 int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor offsets,
@@ -80,7 +81,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_e4m3", &swift::gemm_e4m3);
   m.def("quantize_e4m3", &swift::quantize_e4m3);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
-  m.def("gemm2", &swift::gemm2);
+  m.def("gemm2", &swift::gemm2, pybind11::arg("out"), pybind11::arg("x"), pybind11::arg("w"),
+        pybind11::arg("bias"), pybind11::arg("plan") = -1, pybind11::arg("bn") = 0,
+        pybind11::arg("splits") = 0);
   m.def("gemm2_plan", &swift::gemm2_plan_py);
   m.def("tp_reduce_norm", &swift::tp_reduce_norm);
   m.def("tp_vocab_argmax", &swift::tp_vocab_argmax);

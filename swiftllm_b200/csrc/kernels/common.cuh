@@ -6,6 +6,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
+
 #include <c10/cuda/CUDAStream.h>
 #include <torch/extension.h>
 
@@ -45,6 +48,39 @@ __device__ __forceinline__ void set_status(int* st, int code, int where) {
 }
 
 inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// ---- programmatic dependent launch (PDL)
+// Kernels launched with launch_pdl() may start while the previous kernel on
+// the stream is still finishing; they must call pdl_wait() before touching
+// memory the previous kernel writes (or before any write a previous kernel
+// might still read). pdl_trigger() lets the next PDL kernel start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// SWIFT_PDL=0 turns the overlap off (plain stream order); read once.
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("SWIFT_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SWIFT_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

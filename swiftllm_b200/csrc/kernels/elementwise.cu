@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(1024) norm_kernel(__nv_bfloat16* __restrict__ 
                                                     const __nv_bfloat16* __restrict__ w,
                                                     const __nv_bfloat16* __restrict__ b, int H,
                                                     float eps) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   __shared__ float red[33];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * H;
@@ -114,10 +116,10 @@ static void launch_norm(torch::Tensor out, torch::Tensor x, c10::optional<torch:
   auto st = cur_stream();
   const float e = static_cast<float>(eps);
   switch (per) {
-    case 1: norm_kernel<1, ADD, LN><<<rows, threads, 0, st>>>(op, xp, rp, wp, bp, H, e); break;
-    case 2: norm_kernel<2, ADD, LN><<<rows, threads, 0, st>>>(op, xp, rp, wp, bp, H, e); break;
-    case 3: norm_kernel<3, ADD, LN><<<rows, threads, 0, st>>>(op, xp, rp, wp, bp, H, e); break;
-    case 4: norm_kernel<4, ADD, LN><<<rows, threads, 0, st>>>(op, xp, rp, wp, bp, H, e); break;
+    case 1: launch_pdl(norm_kernel<1, ADD, LN>, dim3(rows), dim3(threads), 0, st, op, xp, rp, wp, bp, H, e); break;
+    case 2: launch_pdl(norm_kernel<2, ADD, LN>, dim3(rows), dim3(threads), 0, st, op, xp, rp, wp, bp, H, e); break;
+    case 3: launch_pdl(norm_kernel<3, ADD, LN>, dim3(rows), dim3(threads), 0, st, op, xp, rp, wp, bp, H, e); break;
+    case 4: launch_pdl(norm_kernel<4, ADD, LN>, dim3(rows), dim3(threads), 0, st, op, xp, rp, wp, bp, H, e); break;
     default: TORCH_CHECK(false, "hidden size too large for the norm kernel");
   }
   SWIFT_CHECK_LAUNCH();
@@ -144,6 +146,8 @@ void fused_add_layer_norm(torch::Tensor out, torch::Tensor x, torch::Tensor resi
 // ---------------------------------------------------------------- activations
 __global__ void silu_mul_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
                                 int64_t rows, int I) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   const int vec = I / 8;
   const int64_t total = rows * vec;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -168,7 +172,7 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x) {
   if (rows == 0) return;
   int64_t total = rows * (I / 8);
   int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
-  silu_mul_kernel<<<blocks, 256, 0, cur_stream()>>>(
+  launch_pdl(silu_mul_kernel, dim3(blocks), dim3(256), 0, cur_stream(), 
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), rows, I);
   SWIFT_CHECK_LAUNCH();
@@ -176,6 +180,8 @@ void silu_and_mul(torch::Tensor out, torch::Tensor x) {
 
 __global__ void gelu_tanh_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
                                  int64_t n8) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8;
        i += (int64_t)gridDim.x * blockDim.x) {
     float v[8], o[8];
@@ -196,7 +202,7 @@ void gelu_tanh(torch::Tensor out, torch::Tensor x) {
   int64_t n8 = x.numel() / 8;
   if (!n8) return;
   int blocks = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, 148 * 16));
-  gelu_tanh_kernel<<<blocks, 256, 0, cur_stream()>>>(
+  launch_pdl(gelu_tanh_kernel, dim3(blocks), dim3(256), 0, cur_stream(), 
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), n8);
   SWIFT_CHECK_LAUNCH();
@@ -206,6 +212,8 @@ void gelu_tanh(torch::Tensor out, torch::Tensor x) {
 __global__ void embedding_kernel(__nv_bfloat16* __restrict__ out, const int32_t* __restrict__ ids,
                                  const __nv_bfloat16* __restrict__ w, int H, int64_t rows_w,
                                  int64_t vocab_start) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   int64_t id = static_cast<int64_t>(ids[t]) - vocab_start;
   bool ok = id >= 0 && id < rows_w;
@@ -221,7 +229,7 @@ void embedding(torch::Tensor out, torch::Tensor ids, torch::Tensor w, int64_t vo
   TORCH_CHECK(H % 8 == 0);
   int64_t T = ids.numel();
   if (!T) return;
-  embedding_kernel<<<T, 128, 0, cur_stream()>>>(
+  launch_pdl(embedding_kernel, dim3(T), dim3(128), 0, cur_stream(), 
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), ids.data_ptr<int32_t>(),
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr<at::BFloat16>()), H, w.size(0), vocab_start);
   SWIFT_CHECK_LAUNCH();
@@ -240,6 +248,8 @@ __global__ void qkv_rope_cache_kernel(__nv_bfloat16* __restrict__ q_out,
                                       int64_t layer_off, int64_t kv_stride, int block_size,
                                       const int32_t* __restrict__ slots, int Hq, int Hkv, int D,
                                       int rot, int max_pos, int* status) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   const int row = (Hq + 2 * Hkv) * D;
   const __nv_bfloat16* src = qkv + t * row;
@@ -315,7 +325,7 @@ void qkv_rope_cache(torch::Tensor q, torch::Tensor qkv, torch::Tensor positions,
   int64_t T = qkv.size(0);
   if (!T) return;
   const int bs = static_cast<int>(kv.size(4));
-  qkv_rope_cache_kernel<<<T, 256, 0, cur_stream()>>>(
+  launch_pdl(qkv_rope_cache_kernel, dim3(T), dim3(256), 0, cur_stream(), 
       reinterpret_cast<__nv_bfloat16*>(q.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr<at::BFloat16>()),
       bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>()) : nullptr,

@@ -860,7 +860,7 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
 
 // ---------------------------------------------------------------- host side
 int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, const torch::Tensor& w,
-                     const __nv_bfloat16* bias);
+                     const __nv_bfloat16* bias, int force, int force_bn, int force_splits);
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1121,9 +1121,14 @@ static int64_t gemm_impl(__nv_bfloat16* y, int64_t ldy, torch::Tensor x, torch::
   const __nv_bfloat16* bp =
       bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
                        : nullptr;
-  // more than 256 tokens: the 2-SM kernel (gemm_2sm.cu), measured faster
-  // than this one-SM kernel at every such Llama projection shape on B200
-  if (T > 256 && sc.k == 0) return gemm2_launch(y, ldy, x, w, bp);
+  // The 2-SM kernel (gemm_2sm.cu) where it measured faster on B200 (graph
+  // replays of back-to-back calls, weights streamed from HBM): every shape
+  // with more than 256 tokens; with at most 256 tokens, weights of >= 12288
+  // rows (data-parallel 256 x 256 pair tiles up to 16384 rows, swapped
+  // operands above). Narrower decode weights stay on the one-SM stream-K
+  // kernel below.
+  if (sc.k == 0 && (T > 256 || M >= 12288))
+    return gemm2_launch(y, ldy, x, w, bp, T > 256 ? -1 : (M > 16384 ? 2 : 0), 0, 1);
   if (gemm_streamk(y, x, w, bp, T, ldx, ldy, 0, 0, sc)) return 1;
   int bn, splits;
   plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);

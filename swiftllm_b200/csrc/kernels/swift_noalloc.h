@@ -20,6 +20,12 @@
 // work overlaps on the GPU (different streams, or different host threads on
 // the same device) race on it and must be serialised by the caller.
 //
+// Failures inside the kernel: a bounded wait inside the kernel that runs out
+// (a copy that never lands) makes it record a code in a second file-scope
+// word and return without hanging; its output is then not valid. Read that
+// word with swift_noalloc_status() after synchronising the stream: code 0
+// means every call since the last clear completed normally.
+//
 // Set-up: the first call on each device looks up the array's device address
 // (cudaGetSymbolAddress, with that device current) and sets the kernels'
 // shared-memory limit; make that first call before any stream capture.
@@ -34,7 +40,9 @@ enum SwiftNoallocStatus {
   SWIFT_NOALLOC_ERR_TOO_LARGE = 1,    // scratch need exceeds SWIFT_NOALLOC_SCRATCH_BYTES
   SWIFT_NOALLOC_ERR_UNSUPPORTED = 2,  // head_dim / block_size / GQA group not supported
   SWIFT_NOALLOC_ERR_CUDA = 3,         // a CUDA runtime call failed (see cudaGetLastError)
-  SWIFT_NOALLOC_ERR_ARGS = 4,         // bad argument (null pointer, non-positive size)
+  SWIFT_NOALLOC_ERR_ARGS = 4,         // bad argument (null pointer, non-positive size,
+                                      // pointer not 16-byte aligned, offset not a
+                                      // multiple of 8 elements)
 };
 
 #ifdef __cplusplus
@@ -54,6 +62,11 @@ int swift_paged_decode_noalloc(void* out, const void* q, const void* kv, int64_t
                                const int32_t* bt, int64_t bt_stride, const int32_t* seq_lens,
                                int rows, int Hq, int Hkv, int splits, float scale, int window,
                                cudaStream_t stream);
+
+// Status word of the allocation-free calls on the current device: *code = 0
+// (no failure), 1 (a bounded wait inside a kernel gave up); *site = where.
+// clear != 0 resets it. Waits for the device; returns a SwiftNoallocStatus.
+int swift_noalloc_status(int* code, int* site, int clear);
 
 #ifdef __cplusplus
 }

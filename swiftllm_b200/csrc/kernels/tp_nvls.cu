@@ -144,6 +144,8 @@ __global__ void __launch_bounds__(kRnThreads)
                           int64_t ctr_off, __nv_bfloat16* __restrict__ residual,
                           const __nv_bfloat16* __restrict__ w, float eps, int T, int H,
                           uint32_t* __restrict__ epochs, int64_t timeout_ns, int* status) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   __shared__ float red[33];
   const uint32_t e = epochs[blockIdx.x];
   if (!rn_barrier<MC>(P, rank, k, ctr_off, (2 * e + 1) * uint32_t(k), timeout_ns, status, 230))
@@ -262,11 +264,11 @@ int64_t tp_reduce_norm(std::vector<int64_t> bases, int64_t mc, int64_t rank, int
   const int64_t tns = static_cast<int64_t>(timeout_s * 1e9);
   auto ep = reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>());
   if (P.mc)
-    tp_reduce_norm_kernel<true><<<kRnBlocks, kRnThreads, 0, cur_stream()>>>(
+    launch_pdl(tp_reduce_norm_kernel<true>, dim3(kRnBlocks), dim3(kRnThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, in_off, out_off, ctr_off, rp, wp, static_cast<float>(eps),
         static_cast<int>(T), static_cast<int>(H), ep, tns, status_word_ptr());
   else
-    tp_reduce_norm_kernel<false><<<kRnBlocks, kRnThreads, 0, cur_stream()>>>(
+    launch_pdl(tp_reduce_norm_kernel<false>, dim3(kRnBlocks), dim3(kRnThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, in_off, out_off, ctr_off, rp, wp, static_cast<float>(eps),
         static_cast<int>(T), static_cast<int>(H), ep, tns, status_word_ptr());
   SWIFT_CHECK_LAUNCH();
@@ -289,6 +291,8 @@ __global__ void __launch_bounds__(kVaThreads)
                            int64_t ld, int V, int v0, int rows, int64_t cand_off, int64_t ctr_off,
                            int32_t* __restrict__ tokens, float* __restrict__ lps,
                            uint32_t* __restrict__ epochs, int64_t timeout_ns, int* status) {
+  pdl_wait();  // previous kernel done (programmatic dependent launch)
+  pdl_trigger();
   __shared__ float sm[32];
   __shared__ int si[32];
   __shared__ float red[33];
@@ -380,12 +384,12 @@ int64_t tp_vocab_argmax(std::vector<int64_t> bases, int64_t mc, int64_t rank, to
   const int64_t tns = static_cast<int64_t>(timeout_s * 1e9);
   auto ep = reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>());
   if (P.mc)
-    tp_vocab_argmax_kernel<true><<<rows, kVaThreads, 0, cur_stream()>>>(
+    launch_pdl(tp_vocab_argmax_kernel<true>, dim3(rows), dim3(kVaThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, logits.data_ptr<float>(), logits.stride(0),
         static_cast<int>(logits.size(1)), static_cast<int>(v0), rows, cand_off, ctr_off,
         tokens.data_ptr<int32_t>(), lps.data_ptr<float>(), ep, tns, status_word_ptr());
   else
-    tp_vocab_argmax_kernel<false><<<rows, kVaThreads, 0, cur_stream()>>>(
+    launch_pdl(tp_vocab_argmax_kernel<false>, dim3(rows), dim3(kVaThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, logits.data_ptr<float>(), logits.stride(0),
         static_cast<int>(logits.size(1)), static_cast<int>(v0), rows, cand_off, ctr_off,
         tokens.data_ptr<int32_t>(), lps.data_ptr<float>(), ep, tns, status_word_ptr());

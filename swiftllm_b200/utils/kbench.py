@@ -55,15 +55,76 @@ def _time(fn, iters=20, flush=True):
     return ts[len(ts) // 2]
 
 
-def gemm_case(T, N, K, once=False, cublas=True, kernel="gemm"):
-    """kernel: "gemm" (the ops.linear dispatch) or "gemm2" (the 2-SM kernel)."""
+def _time_chain(fns, rounds=5):
+    """Back-to-back launches, as in a decode step: ``fns`` (each with its own
+    weights, together larger than L2, so every call streams its weight from
+    HBM) captured once into a CUDA graph, replayed ``rounds`` times inside
+    one event pair; returns ms per call. Host launch cost is excluded, as
+    in the engine's graph replays."""
+    for f in fns:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for f in fns:
+                f()
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for _ in range(rounds):
+        g.replay()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / (rounds * len(fns))
+
+
+def gemm_chain_case(T, N, K):
+    """Decode-style GEMM timing: many back-to-back calls cycling through
+    weight copies totalling > 256 MB; ours (ops.linear dispatch and the 2-SM
+    kernel) vs cuBLAS, ms per call."""
+    C = cuda_ext()
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    n_w = max(2, (256 << 20) // (N * K * 2) + 1)
+    ws = [(torch.randn(N, K, device="cuda") * 0.02).bfloat16() for _ in range(n_w)]
+    y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+    t_ours = _time_chain([lambda w=w: C.gemm(y, x, w, None) for w in ws])
+    t_g2 = _time_chain([lambda w=w: C.gemm2(y, x, w, None) for w in ws])
+    t_dp = _time_chain([lambda w=w: C.gemm2(y, x, w, None, 0) for w in ws])
+    t_cb = _time_chain([lambda w=w: torch.matmul(x, w.t(), out=y) for w in ws])
+    t_pk = None
+    if T <= 256 and N % 128 == 0 and K % 64 == 0:
+        # tile-packed weights: every 128 x 64 tile one contiguous 16 KB block
+        wps = [w.view(N // 128, 128, K // 64, 64).permute(0, 2, 1, 3).contiguous() for w in ws]
+        t_pk = _time_chain([lambda w=w: C.gemm_packed(y, x, w, N, None) for w in wps])
+    pk = measured_peaks()
+    byts = N * K * 2
+    return {"op": "gemm_chain", "T": T, "N": N, "K": K, "ours_us": round(t_ours * 1e3, 1),
+            "gemm2_us": round(t_g2 * 1e3, 1), "gemm2_dp_us": round(t_dp * 1e3, 1),
+            "cublas_us": round(t_cb * 1e3, 1),
+            "packed_1sm_us": round(t_pk * 1e3, 1) if t_pk else None,
+            "ours_weight_TB/s": round(byts / t_ours / 1e9, 2),
+            "ours_frac_bw": round(byts / t_ours / 1e9 / (pk["hbm_gbs"] / 1e3), 3),
+            "plan": C.gemm_plan(N, T, K), "gemm2_plan": C.gemm2_plan(N, T, K)}
+
+
+def gemm_case(T, N, K, once=False, cublas=True, kernel="gemm", plan=(-1, 0, 0)):
+    """kernel: "gemm" (the ops.linear dispatch) or "gemm2" (the 2-SM kernel,
+    with an explicit (plan, bn, splits) when plan[0] >= 0)."""
     C = cuda_ext()
     x = torch.randn(T, K, device="cuda").bfloat16()
     w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
     y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
     if once:
         for _ in range(4):
-            getattr(C, kernel)(y, x, w, None)
+            if kernel == "gemm2":
+                C.gemm2(y, x, w, None, *plan)
+            else:
+                C.gemm(y, x, w, None)
         torch.cuda.synchronize()
         return {}
     pk = measured_peaks()
@@ -217,12 +278,15 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "decode", "prefill", "sweep", "step", "fp8"])
+    ap.add_argument("op", choices=["gemm", "gemmchain", "decode", "prefill", "sweep", "step", "fp8"])
     ap.add_argument("--model", default="llama-2-7b")
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
     ap.add_argument("--splits", type=int, default=1)
     ap.add_argument("--once", action="store_true")
+    ap.add_argument("--plan", default="-1,0,0", help="gemm2 plan,bn,splits (plan -1: automatic)")
+    ap.add_argument("--kernel", default="gemm", choices=["gemm", "gemm2"],
+                    help="gemm: the ops.linear dispatch; gemm2: the 2-SM kernel directly")
     ap.add_argument("--json", default=None)
     a = ap.parse_args(argv)
     if a.op == "sweep":
@@ -236,7 +300,10 @@ def main(argv=None):
     else:
         shp = [int(v) for v in a.shape.split(",")]
         if a.op == "gemm":
-            res = gemm_case(*shp, once=a.once)
+            res = gemm_case(*shp, once=a.once, kernel=a.kernel,
+                            plan=tuple(int(v) for v in a.plan.split(",")))
+        elif a.op == "gemmchain":
+            res = gemm_chain_case(*shp)
         elif a.op == "step":
             res = step_case(*shp, model=a.model, eager=a.eager, once=a.once)
         elif a.op == "decode":

@@ -1,7 +1,8 @@
 """2-SM tcgen05 GEMM (cta_group::2, CTA pairs) against an fp32 PyTorch
 reference: token counts that leave ragged tiles (1, 5, 208, 300, 832),
-feature counts that are not multiples of the 256-row pair tile, split-K,
-bias and a strided output."""
+feature counts that are not multiples of the 256-row pair tile, stream-K
+tiles split over many CTA pairs (run twice: the tile counters reset
+themselves), split-K, bias and a strided output."""
 
 import math
 
@@ -22,23 +23,31 @@ def bf(*shape, scale=1.0):
 
 
 @pytest.mark.parametrize("T,M,K", [(1, 256, 64), (5, 640, 200), (16, 384, 4096), (208, 1000, 512),
+                                   (64, 512, 4096), (256, 4096, 11008), (100, 32000, 1024),
                                    (256, 12288, 4096), (300, 4096, 1024), (832, 4096, 4096),
                                    (1000, 2048, 1000), (4096, 1536, 256)])
 def test_gemm2(C, T, M, K):
     x, w, b = bf(T, K, scale=0.5), bf(M, K, scale=0.05), bf(M)
     big = torch.zeros(T, M + 64, dtype=torch.bfloat16, device="cuda")
     out = big[:, 32:32 + M]
-    for use_bias in (False, True):
-        C.gemm2(out, x, w, b if use_bias else None)
-        r = x.float() @ w.float().t() + (b.float() if use_bias else 0)
-        torch.testing.assert_close(out.float(), r, rtol=2e-2, atol=2e-2 * math.sqrt(K / 64) * 0.5)
+    # automatic plan, data-parallel, and for one token tile stream-K and
+    # swapped operands (tokens as the A operand)
+    plans = [-1, 0] + ([1, 2] if T <= 256 else [])
+    for plan in plans:
+        for use_bias in (False, True):
+            out.fill_(float("nan"))
+            C.gemm2(out, x, w, b if use_bias else None, plan)
+            r = x.float() @ w.float().t() + (b.float() if use_bias else 0)
+            torch.testing.assert_close(out.float(), r, rtol=2e-2,
+                                       atol=2e-2 * math.sqrt(K / 64) * 0.5, msg=f"plan {plan}")
     assert big[:, :32].abs().sum() == 0 and big[:, 32 + M:].abs().sum() == 0
     st = C.read_status(True)
     assert st[0] == 0, st
 
 
 def test_gemm2_plan(C):
-    bn, s = C.gemm2_plan(12288, 832, 4096)
-    assert bn == 208 and s == 1
-    bn, s = C.gemm2_plan(4096, 16, 4096)
-    assert bn == 16 and s > 1
+    bn, s, per, pairs, swap = C.gemm2_plan(12288, 832, 4096)
+    assert bn == 208 and s == 1 and per == 0 and swap == 0
+    # decode: tokens as A, feature tiles spread over every SM pair
+    bn, s, per, pairs, swap = C.gemm2_plan(12288, 256, 4096)
+    assert swap == 1 and bn % 16 == 0 and pairs * bn >= 12288 and pairs <= 74

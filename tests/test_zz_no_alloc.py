@@ -62,6 +62,10 @@ def _run_both(fn, C, lens, Hq, Hkv, D, splits, layer, seed):
     torch.cuda.synchronize()
     assert rc == 0
     torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+    lib = ctypes.CDLL(C.__file__)
+    code, site = ctypes.c_int(-1), ctypes.c_int(-1)
+    assert lib.swift_noalloc_status(ctypes.byref(code), ctypes.byref(site), 1) == 0
+    assert code.value == 0, (code.value, site.value)
 
 
 def test_noalloc_decode_matches_regular_entry_twice():
@@ -79,7 +83,29 @@ def test_noalloc_rejects_oversized_request():
     fn = _lib()
     # rows * Hq * splits * (D + 2) * 4 bytes far above the 8 MiB scratch
     dummy = torch.zeros(16, dtype=torch.int32, device="cuda")
-    rc = fn(dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), 1, 0, 1, 16, 128,
+    rc = fn(dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), 8, 0, 8, 16, 128,
             dummy.data_ptr(), 1, dummy.data_ptr(), 4096, 64, 8, 16, 1.0, 0,
             torch.cuda.current_stream().cuda_stream)
     assert rc == 1
+
+
+def test_noalloc_rejects_unaligned_arguments():
+    fn = _lib()
+    dummy = torch.zeros(64, dtype=torch.int32, device="cuda")
+    p = dummy.data_ptr()
+    stream = torch.cuda.current_stream().cuda_stream
+    # a KV pointer off the 16-byte grid, then a stride that is not a
+    # multiple of 8 elements: rejected before any launch
+    assert fn(p, p, p + 2, 8, 0, 8, 16, 128, p, 1, p, 1, 8, 8, 1, 1.0, 0, stream) == 4
+    assert fn(p, p, p, 12, 0, 8, 16, 128, p, 1, p, 1, 8, 8, 1, 1.0, 0, stream) == 4
+
+
+def test_noalloc_status_word_reads_clean():
+    from swiftllm_b200.ops import cuda_ext
+    lib = ctypes.CDLL(cuda_ext().__file__)
+    st = lib.swift_noalloc_status
+    st.restype = ctypes.c_int
+    st.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    code, site = ctypes.c_int(-1), ctypes.c_int(-1)
+    assert st(ctypes.byref(code), ctypes.byref(site), 1) == 0
+    assert code.value == 0
