@@ -266,9 +266,16 @@ static void launch_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv,
   SWIFT_CHECK_LAUNCH();
 }
 
+bool paged_prefill_tc_supported(int D, int block_size, int Hq, int Hkv);
+void paged_prefill_tc(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
+                      torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int seq0,
+                      int seq1, int max_q_len, double scale, int window);
+
+// impl: -1 the tcgen05 kernel (attention_prefill_tc.cu) where it applies
+// (head_dim 128, 16-token pages), else this one; 0 this one; 1 tcgen05.
 void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                    torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int64_t seq0,
-                   int64_t seq1, int64_t max_q_len, double scale, int64_t window) {
+                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl) {
   CHECK_BF16(q);
   CHECK_BF16(kv);
   CHECK_CONTIG(kv);
@@ -277,6 +284,13 @@ void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t
   const int D = static_cast<int>(q.size(2));
   const int w = static_cast<int>(window);
   const int a = static_cast<int>(seq0), b = static_cast<int>(seq1), mq = static_cast<int>(max_q_len);
+  const bool tc_ok = paged_prefill_tc_supported(D, static_cast<int>(kv.size(4)),
+                                                static_cast<int>(q.size(1)), static_cast<int>(kv.size(3)));
+  TORCH_CHECK(impl != 1 || tc_ok, "paged_prefill: the tcgen05 kernel needs head_dim 128 and 16-token pages");
+  if (impl != 0 && tc_ok) {
+    paged_prefill_tc(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w);
+    return;
+  }
   switch (D) {
     case 64: launch_prefill<64>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;
     case 80: launch_prefill<80>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;

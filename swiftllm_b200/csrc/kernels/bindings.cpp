@@ -27,7 +27,7 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
                      double scale, int64_t window, torch::Tensor ws);
 void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                    torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int64_t seq0,
-                   int64_t seq1, int64_t max_q_len, double scale, int64_t window);
+                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl);
 void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,
             torch::Tensor iparams, torch::Tensor keys, bool any_random);
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
@@ -72,7 +72,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("init_normal", &swift::init_normal);
   m.def("read_status", &swift::read_status, pybind11::arg("clear") = true);
   m.def("paged_decode", &swift::paged_decode);
-  m.def("paged_prefill", &swift::paged_prefill);
+  m.def("paged_prefill", &swift::paged_prefill, pybind11::arg("out"), pybind11::arg("q"),
+        pybind11::arg("kv"), pybind11::arg("layer"), pybind11::arg("bt"), pybind11::arg("q_start"),
+        pybind11::arg("seq_lens"), pybind11::arg("seq0"), pybind11::arg("seq1"),
+        pybind11::arg("max_q_len"), pybind11::arg("scale"), pybind11::arg("window"),
+        pybind11::arg("impl") = -1);
   m.def("sample", &swift::sample);
   m.def("gemm", &swift::gemm);
   m.def("gemm_plan", &swift::gemm_plan);

@@ -177,17 +177,20 @@ def prefill_case(S, L, Hq, Hkv, once=False, D=128):
     qs = torch.arange(0, S * L + 1, L, dtype=torch.int32, device="cuda")
     sl = torch.full((S,), L, dtype=torch.int32, device="cuda")
     out = torch.empty_like(q)
-    fn = lambda: C.paged_prefill(out, q, kv, 0, bt, qs, sl, 0, S, L, 1 / math.sqrt(D), 0)  # noqa: E731
+    fn = lambda impl=-1: C.paged_prefill(out, q, kv, 0, bt, qs, sl, 0, S, L, 1 / math.sqrt(D), 0,  # noqa: E731
+                                         impl)
     if once:
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
         return {}
     ms = _time(fn)
+    ms_old = _time(lambda: fn(0))
     fl = 4.0 * S * Hq * D * L * L / 2  # causal
     pk = measured_peaks()
     return {"op": "paged_prefill", "S": S, "L": L, "Hq": Hq, "Hkv": Hkv, "ms": round(ms, 4),
-            "TFLOP/s": round(fl / ms / 1e9, 1), "frac_flops": round(fl / ms / 1e9 / pk["bf16_tflops"], 3)}
+            "TFLOP/s": round(fl / ms / 1e9, 1), "frac_flops": round(fl / ms / 1e9 / pk["bf16_tflops"], 3),
+            "mma_sync_ms": round(ms_old, 4)}
 
 
 def step_case(S, ctx, model="llama-2-7b", eager=False, once=False, iters=20):

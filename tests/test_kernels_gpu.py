@@ -148,22 +148,40 @@ def test_paged_decode_window(C):
     torch.testing.assert_close(out.float().cpu(), r, rtol=2e-2, atol=2e-2)
 
 
-@pytest.mark.parametrize("Hq,Hkv,D", [(32, 32, 128), (32, 8, 128), (4, 2, 64), (8, 8, 80)])
-def test_paged_prefill(C, Hq, Hkv, D):
-    # (seq_len, q_len): full prompts, chunked prefill with cached prefix, odd tails
-    pairs = [(64, 64), (130, 130), (300, 45), (17, 17), (1, 1), (200, 129)]
+@pytest.mark.parametrize("impl", [0, -1])
+@pytest.mark.parametrize("Hq,Hkv,D", [(32, 32, 128), (32, 8, 128), (64, 8, 128), (8, 2, 128),
+                                      (4, 2, 64), (8, 8, 80)])
+def test_paged_prefill(C, Hq, Hkv, D, impl):
+    # (seq_len, q_len): full prompts, chunked prefill with cached prefix, odd
+    # tails, and prompts spanning several 128-key tiles. impl -1 runs the
+    # tcgen05 kernel for head_dim 128, 0 the mma.sync kernel.
+    pairs = [(64, 64), (130, 130), (300, 45), (17, 17), (1, 1), (200, 129), (700, 700), (600, 300)]
     lens = [p[0] for p in pairs]
     ql = [p[1] for p in pairs]
     kv, bt, q_start, q, sl = _paged_setup(lens, ql, Hq, Hkv, D)
     scale = 1 / math.sqrt(D)
     out = torch.zeros_like(q)
-    C.paged_prefill(out, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 0)
+    C.paged_prefill(out, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 0, impl)
     torch.testing.assert_close(out.float().cpu(), _ref_attn(q, kv, bt, q_start, sl, scale),
                                rtol=2e-2, atol=2e-2)
     out2 = torch.zeros_like(q)
-    C.paged_prefill(out2, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 50)
+    C.paged_prefill(out2, q, kv, 1, bt, q_start, sl, 0, len(lens), max(ql), scale, 50, impl)
     torch.testing.assert_close(out2.float().cpu(), _ref_attn(q, kv, bt, q_start, sl, scale, 50),
                                rtol=2e-2, atol=2e-2)
+    _status_ok(C)
+
+
+def test_paged_prefill_tc_large_logits(C):
+    # logits that grow by far more than 2^8 across key tiles: the tcgen05
+    # kernel must rescale its running output and still match
+    lens, ql = [500, 257], [500, 100]
+    kv, bt, q_start, q, sl = _paged_setup(lens, ql, 16, 4, 128)
+    q = (q.float() * 6.0).to(torch.bfloat16)
+    scale = 1 / math.sqrt(128)
+    out = torch.zeros_like(q)
+    C.paged_prefill(out, q, kv, 1, bt, q_start, sl, 0, 2, max(ql), scale, 0, 1)
+    torch.testing.assert_close(out.float().cpu(), _ref_attn(q, kv, bt, q_start, sl, scale),
+                               rtol=3e-2, atol=3e-2)
     _status_ok(C)
 
 
