@@ -69,5 +69,6 @@ setup(
     packages=["swiftllm_b200", "swiftllm"],
     ext_modules=exts,
     cmdclass=cmdclass,
-    entry_points={"console_scripts": ["swiftllm=swiftllm_b200.cli:main"]},
+    entry_points={"console_scripts": ["swiftllm=swiftllm_b200.cli:main",
+                                     "swiftllm-server=swiftllm_b200.server.__main__:main"]},
 )

@@ -40,6 +40,7 @@ class QuantizationMethod(Enum):
     SQUEEZELLM = "squeezellm"
     GGUF = "gguf"
     FP8 = "fp8"
+    INT8 = "int8"
 
 
 class SchedulerPolicy(Enum):

@@ -48,8 +48,8 @@ constexpr int kHalf = 128 * 64 * 2;        // one 128-row x 64-column bf16 half:
 constexpr int kQBytes = 2 * kHalf;         // 32 KB
 constexpr int kKVStage = 4 * kHalf;        // K (2 halves) + V (2 halves): 64 KB
 constexpr int kStages = 2;
-constexpr int kPBytes = 2 * kHalf;         // 32 KB
-constexpr size_t kSmem = 1024 + kQBytes + size_t(kStages) * kKVStage + kPBytes + 256;
+constexpr int kPBytes = 2 * kHalf;         // 32 KB per P buffer (two buffers)
+constexpr size_t kSmem = 1024 + kQBytes + size_t(kStages) * kKVStage + 2 * kPBytes + 256;
 constexpr float kRescaleLog2 = 8.f;        // raise the P reference max past 2^8 growth only
 
 __device__ __forceinline__ void tma2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
@@ -193,15 +193,16 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
   uint8_t* sQ = base;
   uint8_t* sKV = base + kQBytes;
   uint8_t* sP = sKV + kStages * kKVStage;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kPBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;     // [2]
-  uint64_t* kv_empty = bars + 3;    // [2]
-  uint64_t* s_full = bars + 5;      // [2]
-  uint64_t* s_empty = bars + 7;     // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* k_full = bars + 1;      // [2] per KV stage
+  uint64_t* v_full = bars + 3;      // [2]
+  uint64_t* kv_empty = bars + 5;    // [2]
+  uint64_t* s_full = bars + 7;      // [2] per S accumulator
+  uint64_t* s_empty = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;     // [2] per P buffer
+  uint64_t* o_done = bars + 13;     // [2] per P buffer: the P.V that read it finished
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -224,13 +225,14 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 4);
+      mbar_init(&p_full[s], 4);
+      mbar_init(&o_done[s], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -251,6 +253,18 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
       // Q: 128 rows = P positions x G heads, two 64-column halves
       mbar_arrive_expect_tx(q_full, kQBytes);
       for (int hf = 0; hf < 2; ++hf) tma3d(sQ + hf * kHalf, &tm_q, hf * 64, h * G, qs + p0, q_full);
+      // block ids of the next tile's pages are read while this tile's
+      // stage is awaited
+      int blk[kBN / kPage];
+      auto fetch_ids = [&](int t) {
+#pragma unroll
+        for (int pg = 0; pg < kBN / kPage; ++pg) {
+          const int key = (j0 + t) * kBN + pg * kPage;
+          // pages past the sequence end: any valid block (masked later)
+          blk[pg] = mybt[min(key, L - 1) / kPage];
+        }
+      };
+      if (nt > 0) fetch_ids(0);
       for (int t = 0; t < nt && ok; ++t) {
         const int st = t & 1;
         if (!pft::wait_bar(&kv_empty[st], ((t >> 1) & 1) ^ 1, abort_flag, status, 60)) {
@@ -258,28 +272,30 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
           break;
         }
         uint8_t* kvs = sKV + st * kKVStage;  // K half 0 | K half 1 | V half 0 | V half 1
-        mbar_arrive_expect_tx(&kv_full[st], kKVStage);
-        const int key0 = (j0 + t) * kBN;
+        mbar_arrive_expect_tx(&k_full[st], 2 * kHalf);
+#pragma unroll
         for (int pg = 0; pg < kBN / kPage; ++pg) {
-          int key = key0 + pg * kPage;
-          // pages past the sequence end: any valid block (masked later)
-          const int blk = mybt[min(key, L - 1) / kPage];
-          const int row = blk * rows_per_blk + layer_row_off + h * kPage;  // K rows
-          const int vrow = row + Hkv * kPage;                             // V rows
-          for (int hf = 0; hf < 2; ++hf) {
-            tma2d(kvs + hf * kHalf + pg * kPage * 128, &tm_kv, hf * 64, row, &kv_full[st]);
-            tma2d(kvs + (2 + hf) * kHalf + pg * kPage * 128, &tm_kv, hf * 64, vrow, &kv_full[st]);
-          }
+          const int row = blk[pg] * rows_per_blk + layer_row_off + h * kPage;  // K rows
+          for (int hf = 0; hf < 2; ++hf)
+            tma2d(kvs + hf * kHalf + pg * kPage * 128, &tm_kv, hf * 64, row, &k_full[st]);
         }
+        mbar_arrive_expect_tx(&v_full[st], 2 * kHalf);
+#pragma unroll
+        for (int pg = 0; pg < kBN / kPage; ++pg) {
+          const int vrow = blk[pg] * rows_per_blk + layer_row_off + (Hkv + h) * kPage;  // V rows
+          for (int hf = 0; hf < 2; ++hf)
+            tma2d(kvs + (2 + hf) * kHalf + pg * kPage * 128, &tm_kv, hf * 64, vrow, &v_full[st]);
+        }
+        if (t + 1 < nt) fetch_ids(t + 1);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       bool ok = pft::wait_bar(q_full, 0, abort_flag, status, 61);
-      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
+      const uint32_t qa = smem_u32(sQ);
       auto issue_s = [&](int t) {  // S_t = Q K_t^T into S[t & 1]
         const int st = t & 1;
-        if (!pft::wait_bar(&kv_full[st], (t >> 1) & 1, abort_flag, status, 62)) return false;
+        if (!pft::wait_bar(&k_full[st], (t >> 1) & 1, abort_flag, status, 62)) return false;
         if (!pft::wait_bar(&s_empty[st], ((t >> 1) & 1) ^ 1, abort_flag, status, 63)) return false;
         fence_after();
         const uint32_t ka = smem_u32(sKV + st * kKVStage);
@@ -293,10 +309,12 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
         return true;
       };
       auto issue_pv = [&](int t) {  // O += P_t V_t
-        const int st = t & 1;
-        if (!pft::wait_bar(p_full, t & 1, abort_flag, status, 64)) return false;
+        const int st = t & 1;  // KV stage and P buffer
+        if (!pft::wait_bar(&p_full[st], (t >> 1) & 1, abort_flag, status, 64)) return false;
+        if (!pft::wait_bar(&v_full[st], (t >> 1) & 1, abort_flag, status, 68)) return false;
         fence_after();
         const uint32_t va = smem_u32(sKV + st * kKVStage + 2 * kHalf);
+        const uint32_t pa = smem_u32(sP + st * kPBytes);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
           const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;   // P: K-major, keys
@@ -304,7 +322,7 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
           mma(tO, pft::desc_k(pa + poff), pft::desc_mn(va + voff, kHalf), idesc(true),
               (t > 0 || kk > 0) ? 1u : 0u);
         }
-        commit(o_done);
+        commit(&o_done[st]);
         commit(&kv_empty[st]);
         return true;
       };
@@ -336,10 +354,18 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
       // pass 1: masked, scaled row maximum of this tile
       float mt = -INFINITY;
 #pragma unroll 1
-      for (int c = 0; c < kBN; c += 32) {
-        uint32_t u[32];
+      for (int c = 0; c < kBN; c += 64) {
+        uint32_t u[32], u2[32];
         pft::ld32(tS + c, u);
+        pft::ld32(tS + c + 32, u2);
         pft::ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = key0 + c + 32 + i;
+          const bool keep =
+              row_valid && key <= qpos && key < L && (window <= 0 || key > qpos - window);
+          if (keep) mt = fmaxf(mt, __uint_as_float(u2[i]) * sl2);
+        }
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int key = key0 + c + i;
@@ -349,8 +375,8 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
         }
       }
       m_run = fmaxf(m_run, mt);
-      // P buffer free and O stable: the previous P.V finished
-      if (t > 0 && !pft::wait_bar_warp(o_done, (t - 1) & 1, abort_flag, status, 66)) {
+      // P buffer t & 1 free: the P.V of tile t - 2 finished
+      if (t > 1 && !pft::wait_bar_warp(&o_done[st], ((t - 2) >> 1) & 1, abort_flag, status, 66)) {
         ok = false;
         break;
       }
@@ -367,6 +393,11 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
         m_used = m_run;
       }
       if (__any_sync(0xffffffffu, need)) {
+        // O stable: the P.V of tile t - 1 finished
+        if (!pft::wait_bar_warp(&o_done[(t - 1) & 1], ((t - 1) >> 1) & 1, abort_flag, status, 69)) {
+          ok = false;
+          break;
+        }
         fence_after();
 #pragma unroll 1
         for (int c = 0; c < kD; c += 32) {
@@ -400,7 +431,8 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
           }
           const int chunk = (c >> 3) + ch;  // 0..15
           const int hf = chunk >> 3, c16 = (chunk & 7) ^ (r & 7);
-          store8(reinterpret_cast<__nv_bfloat16*>(sP + hf * kHalf + r * 128 + c16 * 16), e);
+          store8(reinterpret_cast<__nv_bfloat16*>(sP + st * kPBytes + hf * kHalf + r * 128 + c16 * 16),
+                 e);
         }
       }
       fence_before();
@@ -410,10 +442,11 @@ __global__ void __launch_bounds__(pft::kThreads, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[st]);
     }
     // epilogue: wait for the last P.V, O / l, one 256-byte row per thread
-    if (ok && nt > 0 && pft::wait_bar_warp(o_done, (nt - 1) & 1, abort_flag, status, 67)) {
+    if (ok && nt > 0 &&
+        pft::wait_bar_warp(&o_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, abort_flag, status, 67)) {
       fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = out + (int64_t(qs + p0 + p) * Hq + h * G + g) * kD;

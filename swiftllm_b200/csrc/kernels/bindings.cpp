@@ -31,9 +31,14 @@ void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t
 void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,
             torch::Tensor iparams, torch::Tensor keys, bool any_random);
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
+void apply_penalties(torch::Tensor logits, torch::Tensor offsets, torch::Tensor tokens,
+                     torch::Tensor out_counts, torch::Tensor fparams);
 std::vector<int64_t> gemm_plan(int64_t M, int64_t N, int64_t K);
 void gemm_streamk_config(int64_t mode, int64_t mt, int64_t min_per);
 void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x);
+void quantize_s8(torch::Tensor q, torch::Tensor scale, torch::Tensor x);
+int64_t gemm_s8(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                torch::Tensor wscale, c10::optional<torch::Tensor> bias);
 int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
                   torch::Tensor wscale, c10::optional<torch::Tensor> bias);
 int64_t gemm_packed(torch::Tensor out, torch::Tensor x, torch::Tensor wp, int64_t M,
@@ -48,6 +53,7 @@ int64_t tp_vocab_argmax(std::vector<int64_t> bases, int64_t mc, int64_t rank, to
 int64_t gemm2(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias,
               int64_t plan, int64_t bn, int64_t splits);
 std::vector<int64_t> gemm2_plan_py(int64_t M, int64_t N, int64_t K);
+int64_t gemm_swiglu(torch::Tensor out, torch::Tensor x, torch::Tensor w13);
 void flag_wait_probe(torch::Tensor flag, int64_t want, double timeout_s);
 int64_t gemm_grouped(torch::Tensor out, torch::Tensor x, torch::Tensor w, torch::Tensor offsets,
                      int64_t avg_rows);
@@ -78,17 +84,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("max_q_len"), pybind11::arg("scale"), pybind11::arg("window"),
         pybind11::arg("impl") = -1);
   m.def("sample", &swift::sample);
+  m.def("apply_penalties", &swift::apply_penalties);
   m.def("gemm", &swift::gemm);
   m.def("gemm_plan", &swift::gemm_plan);
   m.def("gemm_streamk_config", &swift::gemm_streamk_config);
   m.def("gemm_packed", &swift::gemm_packed);
   m.def("gemm_e4m3", &swift::gemm_e4m3);
   m.def("quantize_e4m3", &swift::quantize_e4m3);
+  m.def("quantize_s8", &swift::quantize_s8);
+  m.def("gemm_s8", &swift::gemm_s8);
   m.def("flag_wait_probe", &swift::flag_wait_probe);
   m.def("gemm2", &swift::gemm2, pybind11::arg("out"), pybind11::arg("x"), pybind11::arg("w"),
         pybind11::arg("bias"), pybind11::arg("plan") = -1, pybind11::arg("bn") = 0,
         pybind11::arg("splits") = 0);
   m.def("gemm2_plan", &swift::gemm2_plan_py);
+  m.def("gemm_swiglu", &swift::gemm_swiglu);
   m.def("tp_reduce_norm", &swift::tp_reduce_norm);
   m.def("tp_vocab_argmax", &swift::tp_vocab_argmax);
   m.def("gemm_grouped", &swift::gemm_grouped);

@@ -247,23 +247,25 @@ __global__ void qkv_rope_cache_kernel(__nv_bfloat16* __restrict__ q_out,
                                       __nv_bfloat16* __restrict__ kv, int64_t blk_stride,
                                       int64_t layer_off, int64_t kv_stride, int block_size,
                                       const int32_t* __restrict__ slots, int Hq, int Hkv, int D,
-                                      int rot, int max_pos, int* status) {
+                                      int rot, int max_pos, int64_t num_slots, int* status) {
   pdl_wait();  // previous kernel done (programmatic dependent launch)
   pdl_trigger();
   const int64_t t = blockIdx.x;
   const int row = (Hq + 2 * Hkv) * D;
   const __nv_bfloat16* src = qkv + t * row;
   int pos = positions[t];
-#ifdef SWIFT_CHECKS
-  if (pos < 0 || pos >= max_pos) {
-    if (threadIdx.x == 0) set_status(status, kErrBadIndex, 100);
-    return;
-  }
-#endif
+  // index guards (always on, one compare each): a position outside the
+  // RoPE table is clamped and a slot outside the pool is not written; both
+  // are recorded as kErrBadIndex in the status word
+  if ((pos < 0 || pos >= max_pos) && threadIdx.x == 0) set_status(status, kErrBadIndex, 100);
   pos = min(max(pos, 0), max_pos - 1);
   const int half = rot / 2;
   const float* cs = cos_sin + static_cast<int64_t>(pos) * rot;
-  const int slot = slots[t];
+  int slot = slots[t];
+  if (slot >= num_slots) {
+    if (threadIdx.x == 0) set_status(status, kErrBadIndex, 101);
+    slot = -1;
+  }
   const int64_t blk = slot >= 0 ? slot / block_size : 0;
   const int off = slot >= 0 ? slot % block_size : 0;
   __nv_bfloat16* kbase = kv + blk * blk_stride + layer_off;
@@ -333,15 +335,19 @@ void qkv_rope_cache(torch::Tensor q, torch::Tensor qkv, torch::Tensor positions,
       reinterpret_cast<__nv_bfloat16*>(kv.data_ptr<at::BFloat16>()), kv.stride(0),
       layer * kv.stride(1), kv.stride(2), bs, slots.data_ptr<int32_t>(), static_cast<int>(Hq),
       static_cast<int>(Hkv), static_cast<int>(D), static_cast<int>(rot),
-      static_cast<int>(cos_sin.size(0)), status_word_ptr());
+      static_cast<int>(cos_sin.size(0)), static_cast<int64_t>(kv.size(0)) * bs, status_word_ptr());
   SWIFT_CHECK_LAUNCH();
 }
 
 // ---------------------------------------------------------------- copy_blocks
 __global__ void copy_blocks_kernel(uint4* __restrict__ kv, const int32_t* __restrict__ pairs,
-                                   int64_t blk_vec) {
+                                   int64_t blk_vec, int64_t num_blocks, int* status) {
   const int p = blockIdx.y;
   const int64_t src = pairs[2 * p], dst = pairs[2 * p + 1];
+  if (src < 0 || src >= num_blocks || dst < 0 || dst >= num_blocks) {  // index guard
+    if (blockIdx.x == 0 && threadIdx.x == 0) set_status(status, kErrBadIndex, 110);
+    return;
+  }
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < blk_vec;
        i += (int64_t)gridDim.x * blockDim.x)
     kv[dst * blk_vec + i] = kv[src * blk_vec + i];
@@ -356,7 +362,9 @@ void copy_blocks(torch::Tensor kv, torch::Tensor pairs) {
   TORCH_CHECK(bytes % 16 == 0);
   dim3 grid(64, static_cast<unsigned>(n));
   copy_blocks_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<uint4*>(kv.data_ptr()),
-                                                     pairs.data_ptr<int32_t>(), bytes / 16);
+                                                     pairs.data_ptr<int32_t>(), bytes / 16,
+                                                     static_cast<int64_t>(kv.size(0)),
+                                                     status_word_ptr());
   SWIFT_CHECK_LAUNCH();
 }
 

@@ -166,6 +166,9 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// silu(g) * u = g * u / (1 + e^-g)
+__device__ __forceinline__ float silu_mul(float g, float u) { return g * u / (1.f + __expf(-g)); }
+
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -270,7 +273,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::kThreads, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                  const __grid_constant__ CUtensorMap tm_y, __nv_bfloat16* __restrict__ y, int64_t ldy, const __nv_bfloat16* __restrict__ bias,
                  float* __restrict__ ws, int M, int N, int K, int BN, int splits, int sk_per,
-                 float* __restrict__ skws, int* __restrict__ skctr, int vec_out, int* status) {
+                 float* __restrict__ skws, int* __restrict__ skctr, int vec_out, int act,
+                 int* status) {
   using namespace g2;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int sh_ok[2][4];
@@ -535,7 +539,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::kThreads, 1)
           if constexpr (SWAP) {
             // this thread's row is token f (= m0 + lane row); columns are
             // features t0 .. t0 + nvalid - 1
-            if (f < M && nvalid > 0) {
+            if (act && f < M && nvalid > 0) {
+              // interleaved (gate, up) column pairs -> silu(gate) * up, 16 outputs
+              __nv_bfloat16* yr = y + int64_t(f) * ldy + t0 / 2;
+              float o[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) o[i] = silu_mul(v[2 * i], v[2 * i + 1]);
+              if (vec_out && nvalid == 32) {
+                store8(yr, o);
+                store8(yr + 8, o + 8);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                  if (2 * i + 1 < nvalid) yr[i] = __float2bfloat16(o[i]);
+              }
+            } else if (f < M && nvalid > 0) {
               __nv_bfloat16* yr = y + int64_t(f) * ldy + t0;
               if (bias != nullptr) {
 #pragma unroll
@@ -558,6 +576,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::kThreads, 1)
                   if (j < nvalid) yr[j] = __float2bfloat16(v[j]);
               }
             }
+            continue;
+          }
+          if (act) {
+            // lanes hold interleaved (gate, up) feature rows: the even lane
+            // of each pair takes the odd lane's value, outputs feature f / 2
+            float o[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float other = __shfl_xor_sync(0xffffffffu, v[j], 1);
+              o[j] = silu_mul(v[j], other);
+            }
+            __nv_bfloat16* box = stage + (nbox & 1) * kEpiBox;  // [32 tokens][16 outputs]
+            if (lane == 0 && nbox >= 2) g2::tma_store_wait_read1();
+            __syncwarp();
+            if ((lane & 1) == 0) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) box[j * 16 + (lane >> 1)] = __float2bfloat16(o[j]);
+            }
+            __syncwarp();
+            // 32 rows x 32 bytes: lane stores both 16-byte halves of row `lane`
+            const int fo = fbase / 2;
+            if (lane < nvalid && fo < M / 2) {
+              __nv_bfloat16* yr = y + int64_t(t0 + lane) * ldy + fo;
+              if (vec_out) {
+                *reinterpret_cast<uint4*>(yr) = *reinterpret_cast<const uint4*>(box + lane * 16);
+                *reinterpret_cast<uint4*>(yr + 8) = *reinterpret_cast<const uint4*>(box + lane * 16 + 8);
+              } else {
+                for (int i = 0; i < 16 && fo + i < M / 2; ++i) yr[i] = box[lane * 16 + i];
+              }
+            }
+            __syncwarp();
             continue;
           }
           if (splits > 1) {
@@ -770,7 +819,7 @@ void gemm2_plan(int64_t M, int64_t N, int64_t K, int* bn, int* splits, int* sk_p
 // Returns the number of kernels launched.
 int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, const torch::Tensor& w,
                      const __nv_bfloat16* bias, int force = -1, int force_bn = 0,
-                     int force_splits = 0) {
+                     int force_splits = 0, int act = 0) {
   const int64_t K = x.size(-1), T = x.numel() / K, M = w.size(0);
   if (T == 0) return 0;
   const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
@@ -789,10 +838,12 @@ int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, cons
   // A operand boxes are 128 rows per CTA, B operand boxes bn / 2
   CUtensorMap tw = tmap_bf16(w.data_ptr(), M, K, w.stride(0), swap ? bn / 2 : g2::kBM);
   CUtensorMap tx = tmap_bf16(x.data_ptr(), T, K, ldx, swap ? g2::kBM : bn / 2);
-  const int vec_out = (M % 8 == 0 && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) ? 1 : 0;
+  const int64_t out_w = act ? M / 2 : M;  // silu-mul halves the output width
+  const int vec_out = (out_w % 8 == 0 && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0) ? 1 : 0;
+  TORCH_CHECK(!act || (splits == 1 && M % 2 == 0), "gemm2: silu-mul needs whole (gate, up) pairs, no split-K");
   // output boxes of 32 features x 32 tokens, no swizzle (dense 64-byte rows)
   CUtensorMap ty;
-  if (vec_out && !swap) {
+  if (vec_out && !swap && !act) {
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(M), static_cast<cuuint64_t>(T)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(ldy * 2)};
     cuuint32_t box[2] = {32, 32};
@@ -821,11 +872,11 @@ int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, cons
   if (swap)
     launch_pdl(gemm2_kernel<true>, dim3(2 * pairs), dim3(g2::kThreads), g2::kSmemBytes, cur_stream(),
                tw, tx, ty, y, ldy, bias, wsp, static_cast<int>(T), static_cast<int>(M),
-               static_cast<int>(K), bn, 1, 0, skws, skctr, vec_out, status_word_ptr());
+               static_cast<int>(K), bn, 1, 0, skws, skctr, vec_out, act, status_word_ptr());
   else
     launch_pdl(gemm2_kernel<false>, dim3(2 * pairs), dim3(g2::kThreads), g2::kSmemBytes, cur_stream(),
                tw, tx, ty, y, ldy, bias, wsp, static_cast<int>(M), static_cast<int>(T),
-               static_cast<int>(K), bn, splits, sk_per, skws, skctr, vec_out, status_word_ptr());
+               static_cast<int>(K), bn, splits, sk_per, skws, skctr, vec_out, act, status_word_ptr());
   if (splits > 1) {
     TORCH_CHECK(M % 8 == 0 && ldy % 8 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0,
                 "gemm2: split-K needs 8-aligned output rows");
@@ -836,6 +887,25 @@ int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, cons
     return 2;
   }
   return 1;
+}
+
+// Gate/up projection with the SwiGLU activation in the epilogue: w13 rows
+// interleaved (gate_0, up_0, gate_1, up_1, ...), out [T, M / 2] =
+// silu(x . gate^T) * (x . up^T). Swapped operands for at most 256 tokens,
+// data-parallel tiles without split-K above. Returns the launches.
+int64_t gemm_swiglu(torch::Tensor out, torch::Tensor x, torch::Tensor w13) {
+  CHECK_BF16(out);
+  CHECK_BF16(x);
+  CHECK_BF16(w13);
+  const int64_t K = x.size(-1), T = x.numel() / K, M = w13.size(0);
+  TORCH_CHECK(w13.size(1) == K && K % 8 == 0 && M % 2 == 0, "gemm_swiglu: shapes");
+  TORCH_CHECK(x.stride(-1) == 1 && w13.stride(1) == 1 && out.stride(-1) == 1);
+  TORCH_CHECK(out.numel() == T * (M / 2), "gemm_swiglu: out must be [T, M / 2]");
+  const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
+  TORCH_CHECK(ldx % 8 == 0 && w13.stride(0) % 8 == 0);
+  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M / 2;
+  return gemm2_launch(reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), ldy, x, w13,
+                      nullptr, T <= 256 ? 2 : 0, 0, 1, 1);
 }
 
 // Python binding: out [T, M] (row stride may exceed M), x [T, K], w [M, K].

@@ -102,6 +102,20 @@ __device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint
       " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
+// kind::i8 with A and B signed int8 (format code 1), s32 accumulate (c
+// format 2), 32 elements of K per instruction like kind::f8f6f4.
+template <int BN>
+__host__ __device__ constexpr uint32_t instr_desc_s8() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>(kGemmBM >> 4) << 24);
+}
+__device__ __forceinline__ void umma_s8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
@@ -222,7 +236,10 @@ struct GemmSmem {
   static constexpr size_t BYTES = 1024 + size_t(STAGES) * STAGE_BYTES + 256;
 };
 
-template <int BN, int STAGES, bool FP8 = false>
+// Q: 0 bf16 operands; 1 E4M3 (kind::f8f6f4); 2 signed int8 (kind::i8, s32
+// accumulators converted to float in the epilogue). For Q != 0 both
+// operands carry per-row fp32 scales applied in the epilogue.
+template <int BN, int STAGES, int Q = 0>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tm_w,
                         const __grid_constant__ CUtensorMap tm_x, __nv_bfloat16* __restrict__ y,
@@ -234,7 +251,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // FP8 (E4M3 weights and activations, per-row scales): a 128-byte smem row
   // holds 128 elements, so one stage covers 128 of K; scales are applied in
   // the epilogue.
-  constexpr int kBK = FP8 ? 128 : kGemmBK;
+  constexpr int kBK = Q ? 128 : kGemmBK;
   using S = GemmSmem<BN, STAGES>;
   // Grouped mode (goff != nullptr, MoE experts): group g multiplies the token
   // rows [goff[g], goff[g+1]) by weight rows [g*M, (g+1)*M); tiles never
@@ -348,7 +365,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = FP8 ? instr_desc_e4m3<BN>() : instr_desc_bf16<BN>();
+      constexpr uint32_t idesc =
+          Q == 1 ? instr_desc_e4m3<BN>() : Q == 2 ? instr_desc_s8<BN>() : instr_desc_bf16<BN>();
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tc) {
@@ -374,8 +392,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
 #pragma unroll
           for (int j = 0; j < kGemmBK / 16; ++j)  // +32 B along K inside the swizzle atom
-            if constexpr (FP8)
+            if constexpr (Q == 1)
               umma_e4m3(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+            else if constexpr (Q == 2)
+              umma_s8(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
             else
               umma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
           umma_commit(&empty[st]);
@@ -413,8 +433,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int f = m * kGemmBM + q * 32 + lane;
       const float b = (bias != nullptr && f < M && splits == 1) ? __bfloat162float(bias[f]) : 0.f;
-      const float wsf = (FP8 && f < M) ? wscale[f] : 1.f;
-      // FP8: scales applied once per chunk, before the stores (independent loads)
+      const float wsf = (Q && f < M) ? wscale[f] : 1.f;
+      // 8-bit: scales applied once per chunk, before the stores (independent loads)
       auto dq = [&](float a, int) { return a; };
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       if constexpr (BN >= 32) {
@@ -423,7 +443,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           const int t0 = x0 + c * 32;
-          if constexpr (FP8) {
+          if constexpr (Q == 2) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(__float_as_int(v[j]));
+          }
+          if constexpr (Q != 0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] *= wsf * xscale[min(t0 + j, N - 1)];
           }
@@ -446,7 +470,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         float v[16];
         tmem_ld16(tbase, v);
         const int t0 = x0;
-        if constexpr (FP8) {
+        if constexpr (Q == 2) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = static_cast<float>(__float_as_int(v[j]));
+        }
+        if constexpr (Q != 0) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] *= wsf * xscale[min(t0 + j, N - 1)];
         }
@@ -860,7 +888,8 @@ __global__ void splitk_reduce_kernel(__nv_bfloat16* __restrict__ y, int64_t ldy,
 
 // ---------------------------------------------------------------- host side
 int64_t gemm2_launch(__nv_bfloat16* y, int64_t ldy, const torch::Tensor& x, const torch::Tensor& w,
-                     const __nv_bfloat16* bias, int force, int force_bn, int force_splits);
+                     const __nv_bfloat16* bias, int force, int force_bn, int force_splits,
+                     int act);
 
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -901,14 +930,14 @@ static int num_sms() {
   return n[dev];
 }
 
-template <int BN, int STAGES, bool FP8 = false>
+template <int BN, int STAGES, int Q = 0>
 static void launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, __nv_bfloat16* y, int64_t ldy,
                         const __nv_bfloat16* bias, float* ws, int M, int N, int K, int splits,
                         const int32_t* goff = nullptr, int groups = 0,
                         const ScatterDesc& sc = ScatterDesc{}, const float* wscale = nullptr,
                         const float* xscale = nullptr) {
   using S = GemmSmem<BN, STAGES>;
-  auto kern = gemm_tcgen05_kernel<BN, STAGES, FP8>;
+  auto kern = gemm_tcgen05_kernel<BN, STAGES, Q>;
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -1128,7 +1157,7 @@ static int64_t gemm_impl(__nv_bfloat16* y, int64_t ldy, torch::Tensor x, torch::
   // operands above). Narrower decode weights stay on the one-SM stream-K
   // kernel below.
   if (sc.k == 0 && (T > 256 || M >= 12288))
-    return gemm2_launch(y, ldy, x, w, bp, T > 256 ? -1 : (M > 16384 ? 2 : 0), 0, 1);
+    return gemm2_launch(y, ldy, x, w, bp, T > 256 ? -1 : (M > 16384 ? 2 : 0), 0, 1, 0);
   if (gemm_streamk(y, x, w, bp, T, ldx, ldy, 0, 0, sc)) return 1;
   int bn, splits;
   plan(static_cast<int>(M), static_cast<int>(T), static_cast<int>(K), &bn, &splits);
@@ -1235,14 +1264,16 @@ void quantize_e4m3(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
 // out [T, M] bf16 = (xq * xscale) . (wq * wscale)^T (+ bias), on
 // tcgen05.mma kind::f8f6f4. xq [T, K], wq [M, K] uint8 holding E4M3 bits,
 // K a multiple of 16. Returns launches.
-int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
-                  torch::Tensor wscale, c10::optional<torch::Tensor> bias) {
+template <int Q>
+static int64_t gemm_q8(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                       torch::Tensor wscale, c10::optional<torch::Tensor> bias) {
   CHECK_BF16(out);
-  TORCH_CHECK(xq.scalar_type() == at::kByte && wq.scalar_type() == at::kByte);
+  TORCH_CHECK((xq.scalar_type() == at::kByte || xq.scalar_type() == at::kChar) &&
+              (wq.scalar_type() == at::kByte || wq.scalar_type() == at::kChar));
   TORCH_CHECK(xq.is_contiguous() && wq.is_contiguous() && out.stride(-1) == 1);
   TORCH_CHECK(xscale.scalar_type() == at::kFloat && wscale.scalar_type() == at::kFloat);
   const int64_t K = xq.size(-1), T = xq.numel() / K, M = wq.size(0);
-  TORCH_CHECK(wq.size(1) == K && K % 16 == 0, "gemm_e4m3: K must match and be a multiple of 16");
+  TORCH_CHECK(wq.size(1) == K && K % 16 == 0, "8-bit GEMM: K must match and be a multiple of 16");
   TORCH_CHECK(xscale.numel() == T && wscale.numel() == M);
   if (T == 0) return 0;
   const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M;
@@ -1265,11 +1296,11 @@ int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, tor
   const float* xsc = xscale.data_ptr<float>();
   const ScatterDesc none{};
   switch (bn) {
-    case 16: launch_gemm<16, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
-    case 32: launch_gemm<32, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
-    case 64: launch_gemm<64, 8, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
-    case 128: launch_gemm<128, 6, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
-    default: launch_gemm<256, 4, true>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 16: launch_gemm<16, 8, Q>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 32: launch_gemm<32, 8, Q>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 64: launch_gemm<64, 8, Q>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    case 128: launch_gemm<128, 6, Q>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
+    default: launch_gemm<256, 4, Q>(tw, tx, y, ldy, bp, wsp, Mi, Ni, Ki, splits, nullptr, 0, none, wsc, xsc); break;
   }
   if (splits > 1) {
     int64_t n = M * T;
@@ -1279,6 +1310,59 @@ int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, tor
     return 2;
   }
   return 1;
+}
+
+int64_t gemm_e4m3(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                  torch::Tensor wscale, c10::optional<torch::Tensor> bias) {
+  return gemm_q8<1>(out, xq, xscale, wq, wscale, bias);
+}
+
+// out [T, M] bf16 = (xq * xscale) . (wq * wscale)^T (+ bias) on
+// tcgen05.mma kind::i8 (exact int32 accumulation). xq [T, K], wq [M, K]
+// int8 (per-row symmetric), K a multiple of 16. Returns launches.
+int64_t gemm_s8(torch::Tensor out, torch::Tensor xq, torch::Tensor xscale, torch::Tensor wq,
+                torch::Tensor wscale, c10::optional<torch::Tensor> bias) {
+  return gemm_q8<2>(out, xq, xscale, wq, wscale, bias);
+}
+
+// Per-row symmetric int8: scale = max|row| / 127, q = round-to-nearest of
+// x / scale (ties to even), so |q| <= 127.
+__global__ void quantize_s8_kernel(int8_t* __restrict__ q, float* __restrict__ scale,
+                                   const __nv_bfloat16* __restrict__ x, int K, int64_t ldx) {
+  const int64_t r = blockIdx.x;
+  const __nv_bfloat16* row = x + r * ldx;
+  float m = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) m = fmaxf(m, fabsf(__bfloat162float(row[k])));
+  __shared__ float red[32];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x + 31) / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float sc = fmaxf(red[0] / 127.f, 1e-12f);
+  const float inv = 1.f / sc;
+  if (threadIdx.x == 0) scale[r] = sc;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) {
+    const int v = __float2int_rn(__bfloat162float(row[k]) * inv);
+    q[r * K + k] = static_cast<int8_t>(max(-127, min(127, v)));
+  }
+}
+
+void quantize_s8(torch::Tensor q, torch::Tensor scale, torch::Tensor x) {
+  CHECK_BF16(x);
+  TORCH_CHECK(q.scalar_type() == at::kChar && q.is_contiguous() && scale.scalar_type() == at::kFloat);
+  const int64_t K = x.size(-1), R = x.numel() / K;
+  TORCH_CHECK(x.stride(-1) == 1 && q.numel() == R * K && scale.numel() == R);
+  if (R == 0) return;
+  const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
+  quantize_s8_kernel<<<static_cast<unsigned>(R), 256, 0, cur_stream()>>>(
+      q.data_ptr<int8_t>(), scale.data_ptr<float>(),
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()), static_cast<int>(K), ldx);
+  SWIFT_CHECK_LAUNCH();
 }
 
 // [token tile, splits, stream-K features-per-unit / 128 (0: not stream-K),

@@ -186,6 +186,50 @@ __global__ void __launch_bounds__(kSampThreads)
   }
 }
 
+// Repetition / presence / frequency penalties, applied in place to fp32
+// logits rows (one private row per sample row) before sampling, the order
+// of the reference's sampler (sampling/mod.rs: penalties -> temperature ->
+// filters). Row r's history is the CSR slice [offsets[r], offsets[r+1]) of
+// (token, output count) pairs over the distinct tokens of prompt + output:
+// repetition divides positive / multiplies negative logits of every seen
+// token; frequency and presence subtract freq * count + pres for tokens
+// generated at least once (OpenAI semantics).
+__global__ void apply_penalties_kernel(float* __restrict__ logits, int64_t ld, int V,
+                                       const int32_t* __restrict__ offsets,
+                                       const int32_t* __restrict__ tokens,
+                                       const int32_t* __restrict__ out_counts,
+                                       const float* __restrict__ rep, const float* __restrict__ pres,
+                                       const float* __restrict__ freq) {
+  const int r = blockIdx.x;
+  float* row = logits + int64_t(r) * ld;
+  const float rp = rep[r], pp = pres[r], fp = freq[r];
+  for (int i = offsets[r] + threadIdx.x; i < offsets[r + 1]; i += blockDim.x) {
+    const int t = tokens[i];
+    if (t < 0 || t >= V) continue;
+    float v = row[t];
+    if (rp != 1.f) v = v > 0.f ? v / rp : v * rp;
+    const int c = out_counts[i];
+    if (c > 0) v -= fp * static_cast<float>(c) + pp;
+    row[t] = v;
+  }
+}
+
+void apply_penalties(torch::Tensor logits, torch::Tensor offsets, torch::Tensor tokens,
+                     torch::Tensor out_counts, torch::Tensor fparams) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1);
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && tokens.scalar_type() == at::kInt &&
+              out_counts.scalar_type() == at::kInt && fparams.scalar_type() == at::kFloat);
+  const int n = static_cast<int>(logits.size(0));
+  TORCH_CHECK(offsets.numel() == n + 1 && fparams.numel() == 3 * n);
+  if (n == 0) return;
+  const float* fp = fparams.data_ptr<float>();
+  apply_penalties_kernel<<<n, 256, 0, cur_stream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(1)),
+      offsets.data_ptr<int32_t>(), tokens.data_ptr<int32_t>(), out_counts.data_ptr<int32_t>(), fp,
+      fp + n, fp + 2 * n);
+  SWIFT_CHECK_LAUNCH();
+}
+
 // fparams [3, n] = (temperature, top_p, min_p); iparams [4, n] = (logit row,
 // top_k, counter0, counter1); keys [n] (int64 holding the uint64 Philox key).
 void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,

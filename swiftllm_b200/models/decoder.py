@@ -175,7 +175,7 @@ class DecoderModel:
         yield "embed", self.embed
         for i, L in enumerate(self.layers):
             for k, v in vars(L).items():
-                if isinstance(v, ops.Fp8Weight):
+                if isinstance(v, (ops.Fp8Weight, ops.Int8Weight)):
                     yield f"layers.{i}.{k}.q", v.q
                     yield f"layers.{i}.{k}.scale", v.scale
                 elif v is not None:
@@ -242,6 +242,19 @@ class DecoderModel:
             return ("rows", c.vocab_size, [(0, self.vocab_start, self.vocab_end - self.vocab_start)])
         return None
 
+    def quantize_int8(self) -> None:
+        """W8A8: the dense projection weights (QKV, o_proj, gate_up / fc1,
+        down / fc2) become per-output-feature int8; activations are
+        quantized per token at every GEMM. Embedding, norms, LM head and MoE
+        experts stay in the model dtype."""
+        for L in self.layers:
+            for name in ("wqkv", "wo", "w13", "w1", "w2"):
+                w = getattr(L, name, None)
+                if isinstance(w, torch.Tensor) and w.dim() == 2:
+                    setattr(L, name, ops.int8_weight(w))
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
     def quantize_fp8(self) -> None:
         """Replace the dense projection weights (QKV, o_proj, gate_up / fc1,
         down / fc2) by E4M3 weights with per-output-feature scales. The
@@ -253,6 +266,22 @@ class DecoderModel:
                     setattr(L, name, ops.fp8_weight(w))
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
+
+    def fuse_swiglu(self) -> None:
+        """Store every dense gate/up weight interleaved (gate_i, up_i) so the
+        SwiGLU activation runs in the GEMM epilogue (``ops.linear_swiglu``)."""
+        for L in self.layers:
+            w = getattr(L, "w13", None)
+            if isinstance(w, torch.Tensor) and w.dim() == 2 and w.is_cuda:
+                L.w13 = ops.interleave_gate_up(w)
+                L.swiglu_fused = True
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def _gate_up_act(self, L, x: torch.Tensor) -> torch.Tensor:
+        if getattr(L, "swiglu_fused", False):
+            return ops.linear_swiglu(x, L.w13)
+        return ops.silu_and_mul(ops.linear(x, L.w13))
 
     def load_state(self, get: Callable[[str], Optional[torch.Tensor]]) -> None:
         """Fill weights from full (unsharded) HF-named tensors; ``get`` returns a
@@ -297,8 +326,7 @@ class DecoderModel:
             h = ops.linear(x, L.w1, L.b1)
             h = ops.gelu_tanh(h)
             return self.tp.linear_reduce(h, L.w2) if reduce else ops.linear(h, L.w2)
-        h = ops.linear(x, L.w13)
-        h = ops.silu_and_mul(h)
+        h = self._gate_up_act(L, x)
         if reduce:  # down_proj + cross-rank sum
             return self.tp.linear_reduce(h, L.w2)
         return ops.linear(h, L.w2)
@@ -334,8 +362,7 @@ class DecoderModel:
                 ops.linear(g, L.w2, L.b2 if self.tp.rank == 0 else None,
                            out=self.tp.reduce_buffer(T, H))
             else:
-                ops.linear(ops.silu_and_mul(ops.linear(x, L.w13)), L.w2,
-                           out=self.tp.reduce_buffer(T, H))
+                ops.linear(self._gate_up_act(L, x), L.w2, out=self.tp.reduce_buffer(T, H))
             w_next = self.layers[i + 1].ln1 if i + 1 < n else self.norm_w
             x = self.tp.reduce_norm(T, h, w_next, c.rms_norm_eps)
         return x.index_select(0, meta.logits_idx)

@@ -111,6 +111,64 @@ class Fp8Weight:
         return self.q.view(torch.float8_e4m3fn).float() * self.scale[:, None]
 
 
+class Int8Weight:
+    """A linear weight stored as symmetric int8 with one fp32 scale per
+    output feature (W8A8: activations are quantized per token before each
+    GEMM, int32 accumulation on tcgen05 kind::i8)."""
+
+    def __init__(self, q: torch.Tensor, scale: torch.Tensor):
+        self.q = q
+        self.scale = scale
+
+    @property
+    def shape(self):
+        return self.q.shape
+
+    @property
+    def device(self):
+        return self.q.device
+
+    def dequantize(self) -> torch.Tensor:
+        return self.q.float() * self.scale[:, None]
+
+
+def quantize_s8(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-row symmetric int8: (int8 [R, K], fp32 scale [R]), scale =
+    max|row| / 127, round to nearest even."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if not x2.is_cuda:
+        s = (x2.float().abs().amax(-1) / 127.0).clamp_min(1e-12)
+        q = torch.round(x2.float() / s[:, None]).clamp(-127, 127).to(torch.int8)
+        return q, s
+    q = torch.empty(x2.shape, dtype=torch.int8, device=x2.device)
+    s = torch.empty(x2.shape[0], dtype=torch.float32, device=x2.device)
+    cuda_ext().quantize_s8(q, s, x2)
+    _count()
+    return q, s
+
+
+def int8_weight(w: torch.Tensor) -> Int8Weight:
+    q, s = quantize_s8(w)
+    return Int8Weight(q, s)
+
+
+def _linear_int8(x, w: Int8Weight, b, out):
+    xq, xs = quantize_s8(x)
+    if not x.is_cuda:
+        y = (xq.float() * xs[:, None]) @ w.dequantize().t()
+        if b is not None:
+            y = y + b.float()
+        y = y.to(x.dtype).reshape(x.shape[:-1] + (w.shape[0],))
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)
+    _count(cuda_ext().gemm_s8(out, xq, xs, w.q, w.scale, b))
+    return out
+
+
 def quantize_e4m3(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row E4M3 quantisation: (uint8 bits [R, K], fp32 scale [R]),
     scale = max|row| / 448."""
@@ -154,6 +212,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if isinstance(w, Fp8Weight):
         return _linear_fp8(x, w, b, out)
+    if isinstance(w, Int8Weight):
+        return _linear_int8(x, w, b, out)
     if not x.is_cuda:
         return ref.linear(x, w, b)
     if _GEMM_BACKEND == "cublas":
@@ -173,6 +233,25 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
         x = torch.nn.functional.pad(x, (0, pad))
         w = torch.nn.functional.pad(w, (0, pad))
     _count(C.gemm(out, x, w, b))
+    return out
+
+
+def interleave_gate_up(w13: torch.Tensor) -> torch.Tensor:
+    """[gate rows; up rows] -> rows (gate_0, up_0, gate_1, up_1, ...), the
+    layout ``linear_swiglu`` reads."""
+    I = w13.shape[0] // 2
+    return torch.stack((w13[:I], w13[I:]), dim=1).reshape(w13.shape).contiguous()
+
+
+def linear_swiglu(x: torch.Tensor, w13_il: torch.Tensor) -> torch.Tensor:
+    """silu(x . gate^T) * (x . up^T) for an interleaved gate/up weight, the
+    activation applied in the GEMM epilogue (one kernel, [T, I] written)."""
+    if not x.is_cuda:
+        g = ref.linear(x, w13_il[0::2])
+        u = ref.linear(x, w13_il[1::2])
+        return ref.silu_and_mul(torch.cat([g, u], dim=-1))
+    out = torch.empty(x.shape[:-1] + (w13_il.shape[0] // 2,), dtype=x.dtype, device=x.device)
+    _count(cuda_ext().gemm_swiglu(out, x, w13_il))
     return out
 
 

@@ -143,8 +143,14 @@ class ModelRunner:
         q = getattr(self.ecfg.quantization, "value", self.ecfg.quantization)
         if q == "fp8":
             self.model.quantize_fp8()
+        elif q == "int8":
+            self.model.quantize_int8()
         elif q not in (None, "none"):
-            raise NotImplementedError(f"quantization {q!r} is not supported (fp8 is)")
+            raise NotImplementedError(f"quantization {q!r} is not supported (fp8 and int8 are)")
+        elif (self.is_cuda and ops.gemm_backend() == "tcgen05"
+              and os.environ.get("SWIFTLLM_FUSE_SWIGLU", "1") != "0"):
+            # our GEMMs: SwiGLU in the gate/up GEMM epilogue
+            self.model.fuse_swiglu()
         if self.is_cuda:
             torch.cuda.synchronize(self.device)
         log.info("weights ready in %.1fs (%s, rank %d/%d)", time.time() - t0, fmt,

@@ -49,38 +49,78 @@ class BatchSampler:
         self.device = torch.device(device)
         self.step = 0
 
+    @staticmethod
+    def penalty_csr(n: int, rep: np.ndarray, pres: np.ndarray, freq: np.ndarray,
+                    hist: Callable[[int], Tuple[np.ndarray, np.ndarray]]):
+        """Per sample row, the distinct tokens a penalty touches with their
+        output counts: (offsets [n + 1], tokens, out_counts) int32. Rows
+        without penalties are empty; presence/frequency only see generated
+        tokens (count > 0), repetition also the prompt's."""
+        offs = np.zeros(n + 1, dtype=np.int32)
+        toks, cnts = [], []
+        for r in range(n):
+            if rep[r] == 1.0 and pres[r] == 0.0 and freq[r] == 0.0:
+                offs[r + 1] = offs[r]
+                continue
+            prompt, output = hist(r)
+            uo, co = np.unique(np.asarray(output, dtype=np.int64), return_counts=True)
+            if rep[r] != 1.0 and len(prompt):
+                up = np.setdiff1d(np.unique(np.asarray(prompt, dtype=np.int64)), uo,
+                                  assume_unique=True)
+                t = np.concatenate([uo, up])
+                c = np.concatenate([co, np.zeros(up.size, dtype=co.dtype)])
+            else:
+                t, c = uo, co
+            toks.append(t.astype(np.int32))
+            cnts.append(c.astype(np.int32))
+            offs[r + 1] = offs[r] + t.size
+        tk = np.concatenate(toks) if toks else np.zeros(0, np.int32)
+        ct = np.concatenate(cnts) if cnts else np.zeros(0, np.int32)
+        return offs, tk, ct
+
     def _penalize(self, logits: torch.Tensor, b, rows: np.ndarray,
                   history: Callable[[int], Tuple[np.ndarray, np.ndarray]]) -> torch.Tensor:
-        """Apply repetition/frequency/presence penalties to the logits rows of
-        ``rows``; history(seq_id) -> (prompt_ids, output_ids)."""
-        rep = np.asarray(b.repetition_penalty)
-        pres = np.asarray(b.presence_penalty)
-        freq = np.asarray(b.frequency_penalty)
+        """Repetition/frequency/presence penalties on a private copy of each
+        sample row's logits; history(seq_id) -> (prompt_ids, output_ids).
+        On the GPU: one gather, one host->device copy of the penalty table
+        (CSR) and one kernel for the whole batch."""
+        rep = np.asarray(b.repetition_penalty, dtype=np.float32)
+        pres = np.asarray(b.presence_penalty, dtype=np.float32)
+        freq = np.asarray(b.frequency_penalty, dtype=np.float32)
         lidx = np.asarray(b.sample_logit_idx)
         tgt = np.asarray(b.sample_target_seq)
-        out = logits[torch.from_numpy(lidx.astype(np.int64)).to(logits.device)].clone()
         seq_ids = np.asarray(b.seq_ids)
         srow = np.asarray(b.sample_seq_row)
-        for r in range(out.shape[0]):
-            if rep[r] == 1.0 and pres[r] == 0.0 and freq[r] == 0.0:
-                continue
-            sid = int(tgt[r]) if tgt[r] >= 0 else int(seq_ids[srow[r]])
-            prompt, output = history(sid)
+        n = lidx.shape[0]
+        sid = lambda r: int(tgt[r]) if tgt[r] >= 0 else int(seq_ids[srow[r]])  # noqa: E731
+        out = logits.index_select(0, torch.from_numpy(lidx.astype(np.int64)).to(logits.device))
+        offs, tk, ct = self.penalty_csr(n, rep, pres, freq, lambda r: history(sid(r)))
+        if not out.is_cuda:
             V = out.shape[1]
-            row = out[r]
-            if rep[r] != 1.0:
-                seen = np.unique(np.concatenate([prompt, output]).astype(np.int64))
-                seen = seen[(seen >= 0) & (seen < V)]
-                if seen.size:
-                    idx = torch.from_numpy(seen).to(row.device)
-                    v = row[idx]
-                    row[idx] = torch.where(v > 0, v / float(rep[r]), v * float(rep[r]))
-            if output.size and (pres[r] != 0.0 or freq[r] != 0.0):
-                t, c = np.unique(output.astype(np.int64), return_counts=True)
+            for r in range(n):
+                a, e = int(offs[r]), int(offs[r + 1])
+                if a == e:
+                    continue
+                t = torch.from_numpy(tk[a:e].astype(np.int64))
+                c = torch.from_numpy(ct[a:e].astype(np.float32))
                 ok = (t >= 0) & (t < V)
-                idx = torch.from_numpy(t[ok]).to(row.device)
-                cnt = torch.from_numpy(c[ok].astype(np.float32)).to(row.device)
-                row.index_add_(0, idx, -(float(freq[r]) * cnt + float(pres[r])))
+                t, c = t[ok], c[ok]
+                v = out[r, t]
+                if rep[r] != 1.0:
+                    v = torch.where(v > 0, v / float(rep[r]), v * float(rep[r]))
+                v = v - torch.where(c > 0, float(freq[r]) * c + float(pres[r]), torch.zeros_like(c))
+                out[r, t] = v
+            return out
+        from ..ops import cuda_ext
+        dev = out.device
+        ints = torch.from_numpy(np.concatenate([offs, tk, ct]).astype(np.int32)).to(dev, non_blocking=True)
+        fp = torch.from_numpy(np.concatenate([rep, pres, freq]).astype(np.float32)).to(dev, non_blocking=True)
+        o_t = ints[:n + 1]
+        t_t = ints[n + 1:n + 1 + tk.size]
+        c_t = ints[n + 1 + tk.size:]
+        cuda_ext().apply_penalties(out, o_t, t_t, c_t, fp)
+        from .. import ops as _ops
+        _ops._count()
         return out
 
     def __call__(self, logits: torch.Tensor, b,

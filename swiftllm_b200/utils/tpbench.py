@@ -41,6 +41,33 @@ def _time(fn, iters=20):
     return float(t.item())
 
 
+def _time_graph(fn, reps=20):
+    """Per-call time of ``reps`` back-to-back calls captured in one CUDA
+    graph (ranks stay in lock step through the collectives, so one-off
+    launch skew between ranks is excluded); max over ranks."""
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(reps):
+                fn()
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--hidden", type=int, default=4096)
@@ -78,6 +105,10 @@ def main():
                 ops.rms_norm(y, nw, 1e-5, res)
             t_nccl = _time(nccl)
             t_cublas = _time(lambda: torch.matmul(x, w.t(), out=y))
+            # back to back in a graph, as inside a decode step
+            g_comm = _time_graph(lambda: tp.reduce_norm(T, res, nw, 1e-5))
+            g_ours = _time_graph(ours)
+            g_nccl = _time_graph(nccl)
             link_s = (world - 1) / world * T * H * 2 / (LINK_GBS * 1e9)
             if rank == 0:
                 print(json.dumps({"K": K, "T": T, "ours_ms": round(t_ours, 4),
@@ -85,6 +116,9 @@ def main():
                                   "gemm_ms": round(t_gemm, 4),
                                   "cublas_nccl_norm_ms": round(t_nccl, 4),
                                   "cublas_ms": round(t_cublas, 4),
+                                  "graph_reduce_norm_ms": round(g_comm, 4),
+                                  "graph_ours_ms": round(g_ours, 4),
+                                  "graph_cublas_nccl_norm_ms": round(g_nccl, 4),
                                   "reduce_link_roofline_frac": round(link_s * 1e3 / t_comm, 3),
                                   "multimem": bool(tp.mc)}), flush=True)
     st = tp.C.read_status(True)

@@ -51,3 +51,19 @@ def test_gemm2_plan(C):
     # decode: tokens as A, feature tiles spread over every SM pair
     bn, s, per, pairs, swap = C.gemm2_plan(12288, 256, 4096)
     assert swap == 1 and bn % 16 == 0 and pairs * bn >= 12288 and pairs <= 74
+
+
+@pytest.mark.parametrize("T,I,K", [(1, 128, 64), (37, 1376, 512), (256, 11008, 4096), (256, 2752, 4096),
+                                   (300, 5504, 1024), (832, 11008, 4096)])
+def test_gemm_swiglu(C, T, I, K):
+    # gate/up GEMM with silu(gate) * up in the epilogue, interleaved weight
+    from swiftllm_b200 import ops
+    x, w13 = bf(T, K, scale=0.5), bf(2 * I, K, scale=0.05)
+    out = torch.full((T, I), float("nan"), dtype=torch.bfloat16, device="cuda")
+    C.gemm_swiglu(out, x, ops.interleave_gate_up(w13))
+    h = x.float() @ w13.float().t()
+    g, u = h[:, :I], h[:, I:]
+    r = torch.nn.functional.silu(g) * u
+    torch.testing.assert_close(out.float(), r, rtol=3e-2, atol=3e-2 * math.sqrt(K / 64) * 0.5)
+    st = C.read_status(True)
+    assert st[0] == 0, st

@@ -382,3 +382,74 @@ def test_linear_odd_k():
     x, w = bf(19, 172, scale=0.5), bf(96, 172, scale=0.05)
     y = ops.linear(x, w)
     torch.testing.assert_close(y.float(), x.float() @ w.float().t(), rtol=2e-2, atol=2e-2)
+
+
+def test_apply_penalties_kernel(C):
+    # the batched penalty kernel against the same table applied in PyTorch
+    import sys, os
+    sys.path.insert(0, os.path.dirname(__file__))
+    from test_penalties_cpu import _case, apply_csr
+    from swiftllm_b200.sampling.batch import BatchSampler
+    logits, hist, rep, pres, freq = _case(seed=3)
+    n = logits.shape[0]
+    offs, tk, ct = BatchSampler.penalty_csr(n, rep, pres, freq, lambda r: hist[r])
+    want = apply_csr(logits, offs, tk, ct, rep, pres, freq)
+    dev = torch.from_numpy(logits).cuda()
+    C.apply_penalties(dev, torch.from_numpy(offs).cuda(), torch.from_numpy(tk).cuda(),
+                      torch.from_numpy(ct).cuda(), torch.from_numpy(np.concatenate([rep, pres, freq])).cuda())
+    torch.testing.assert_close(dev.cpu(), want, rtol=1e-6, atol=1e-6)
+
+
+def test_index_guards_record_and_skip(C):
+    # out-of-pool slots and block ids are never written: the kernels record
+    # kErrBadIndex (3) in the status word and skip the access
+    from swiftllm_b200.models.rope import cos_sin_table
+    C.read_status(True)
+    Hq, Hkv, D, bs, nb = 4, 2, 64, 16, 4
+    qkv = bf(3, (Hq + 2 * Hkv) * D)
+    pos = torch.tensor([0, 1, 2], dtype=torch.int32, device="cuda")
+    slots = torch.tensor([0, nb * bs + 5, 1], dtype=torch.int32, device="cuda")
+    cs = cos_sin_table(D, 10000.0, 16, device="cuda")
+    kv = torch.zeros(nb, 1, 2, Hkv, bs, D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(3, Hq, D, dtype=torch.bfloat16, device="cuda")
+    C.qkv_rope_cache(q, qkv, pos, cs, kv, 0, slots, Hq, Hkv, D, D, None)
+    torch.cuda.synchronize()
+    st = C.read_status(True)
+    assert st[0] == 3 and st[1] == 101, st
+    assert kv[:, :, :, :, 2:].abs().sum() == 0  # only slots 0 and 1 written
+    kv2 = bf(6, 1, 2, 2, 16, 64)
+    before = kv2.clone()
+    C.copy_blocks(kv2, torch.tensor([[1, 6], [9, 2]], dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    st = C.read_status(True)
+    assert st[0] == 3 and st[1] == 110, st
+    assert torch.equal(kv2, before)
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (37, 640, 256), (256, 12288, 4096),
+                                   (700, 4096, 11008)])
+def test_gemm_s8(C, T, N, K):
+    # W8A8 on tcgen05 kind::i8: int32 accumulation is exact, so the result
+    # matches the dequantised fp32 product up to the bf16 output rounding
+    from swiftllm_b200 import ops
+    x = bf(T, K, scale=0.5)
+    w = bf(N, K, scale=0.05)
+    xq, xs = ops.quantize_s8(x)
+    wq, wsc = ops.quantize_s8(w)
+    xs_ref = (x.float().abs().amax(-1) / 127).clamp_min(1e-12)
+    torch.testing.assert_close(xs, xs_ref, rtol=1e-6, atol=0)
+    out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+    C.gemm_s8(out, xq, xs, wq, wsc, None)
+    r = (xq.float() @ wq.float().t()) * xs[:, None] * wsc[None, :]
+    torch.testing.assert_close(out.float(), r, rtol=1e-2, atol=1e-2)
+    _status_ok(C)
+
+
+def test_int8_model_gpu():
+    from swiftllm_b200 import LLM, SamplingParams
+    sp = SamplingParams(temperature=0, max_tokens=16, ignore_eos=True)
+    llm = LLM("tiny-llama", load_format="dummy", dtype="bfloat16", gpu_memory_utilization=0.3,
+              max_model_len=256, quantization="int8")
+    out = llm.generate(prompt_token_ids=[list(range(100, 164))], sampling_params=sp, use_tqdm=False)
+    assert len(out[0].outputs[0].token_ids) == 16
+    llm.shutdown()
