@@ -178,7 +178,7 @@ class DecoderModel:
                 if isinstance(v, (ops.Fp8Weight, ops.Int8Weight)):
                     yield f"layers.{i}.{k}.q", v.q
                     yield f"layers.{i}.{k}.scale", v.scale
-                elif v is not None:
+                elif isinstance(v, torch.Tensor):
                     yield f"layers.{i}.{k}", v
         yield "norm", self.norm_w
         if self.norm_b is not None:
@@ -266,6 +266,17 @@ class DecoderModel:
                     setattr(L, name, ops.fp8_weight(w))
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
+
+    def pad_k(self) -> None:
+        """Zero-pad every dense projection weight whose input width is not a
+        multiple of 8 (TMA rows must be 16-byte multiples; this happens for
+        odd TP shard widths). Done once here, so a GEMM call pads only its
+        activation."""
+        for L in self.layers:
+            for name in ("wqkv", "wo", "w13", "w1", "w2"):
+                w = getattr(L, name, None)
+                if isinstance(w, torch.Tensor) and w.dim() == 2 and w.shape[1] % 8:
+                    setattr(L, name, torch.nn.functional.pad(w, (0, 8 - w.shape[1] % 8)).contiguous())
 
     def fuse_swiglu(self) -> None:
         """Store every dense gate/up weight interleaved (gate_i, up_i) so the

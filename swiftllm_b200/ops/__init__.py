@@ -217,6 +217,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     if not x.is_cuda:
         return ref.linear(x, w, b)
     if _GEMM_BACKEND == "cublas":
+        if w.shape[1] != x.shape[-1]:  # weight zero-padded at load
+            x = torch.nn.functional.pad(x, (0, w.shape[1] - x.shape[-1]))
         y = torch.nn.functional.linear(x, w, b)
         if out is not None:
             out.copy_(y)
@@ -228,10 +230,15 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
     K = x.shape[-1]
     if K % 8:
         # TMA rows must be 16-byte multiples: zero-pad K (odd shard widths,
-        # e.g. a small FFN split over many ranks)
+        # e.g. a small FFN split over many ranks). Model weights arrive
+        # padded already (DecoderModel.pad_k); only the activation is padded
+        # per call.
         pad = 8 - K % 8
         x = torch.nn.functional.pad(x, (0, pad))
-        w = torch.nn.functional.pad(w, (0, pad))
+        if w.shape[1] == K:
+            w = torch.nn.functional.pad(w, (0, pad))
+    elif w.shape[1] != K:
+        raise ValueError(f"linear: weight K {w.shape[1]} does not match input K {K}")
     _count(C.gemm(out, x, w, b))
     return out
 

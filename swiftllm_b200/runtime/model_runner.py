@@ -152,6 +152,7 @@ class ModelRunner:
             # our GEMMs: SwiGLU in the gate/up GEMM epilogue
             self.model.fuse_swiglu()
         if self.is_cuda:
+            self.model.pad_k()
             torch.cuda.synchronize(self.device)
         log.info("weights ready in %.1fs (%s, rank %d/%d)", time.time() - t0, fmt,
                  self.tp.rank, self.tp.size)
