@@ -393,7 +393,7 @@ def main() -> None:
     ap.add_argument("--workload", default="llama2-7b", choices=sorted(WORKLOADS))
     ap.add_argument("--max-num-seqs", type=int, default=None)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
-    ap.add_argument("--gemm", default="tcgen05", choices=["tcgen05", "cublas"])
+    ap.add_argument("--gemm", default="auto", choices=["auto", "tcgen05", "cublas"])
     ap.add_argument("--baseline", default="run", choices=["run", "skip"],
                     help="also run the cuBLAS + NCCL arm on the same workload (vs_baseline)")
     ap.add_argument("--profile-host", action="store_true",

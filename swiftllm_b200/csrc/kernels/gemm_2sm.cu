@@ -102,6 +102,27 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
   *abort_flag = 1;
   return false;
 }
+// Warp-uniform bounded wait: every lane polls, all agree before leaving.
+__device__ __forceinline__ bool wait_warp_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                   int* status, int where) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    if ((i & 255) == 255 && __any_sync(0xffffffffu, *abort_flag != 0)) return false;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    set_status(status, kErrWaitTimeout, where);
+    *abort_flag = 1;
+  }
+  return false;
+}
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
+}
 // K-major, 128-byte swizzle, 8-row atoms 1024 B apart (SBO), descriptor v1.
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   uint64_t d = 0;
@@ -380,14 +401,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::kThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (leader && lane == 0) {
+    // MMA issue: the whole warp runs the loop with warp-uniform waits and
+    // one elected lane issues the MMAs and commits. (A single-lane loop
+    // beside 31 parked lanes issued measurably slower: about 400 ns per
+    // 64-wide k-step at 64-feature tiles, against 290 ns converged.)
+    if (leader) {
       const uint32_t idesc = idesc_bf16_m256(BN);
       uint32_t it = 0;
       bool ok = true;
       for (int i = 0; i < S.nseg && ok; ++i) {
         const Seg g = S.get(i);
         const uint32_t buf = i & 1;
-        if (!wait_or_abort(&tempty[buf], ((i >> 1) & 1) ^ 1, abort_flag, status, 41, true)) {
+        if (!wait_warp_or_abort(&tempty[buf], ((i >> 1) & 1) ^ 1, abort_flag, status, 41)) {
           ok = false;
           break;
         }
@@ -395,22 +420,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(g2::kThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * buf_cols;
         for (int kk = g.k0; kk < g.k1; ++kk, ++it) {
           const int st = it % kStages;
-          if (!wait_or_abort(&full[st], (it / kStages) & 1, abort_flag, status, 42)) {
+          if (!wait_warp_or_abort(&full[st], (it / kStages) & 1, abort_flag, status, 42)) {
             ok = false;
             break;
           }
           fence_after();
-          const uint32_t a = smem_u32(tiles + size_t(st) * kStageBytes);
-          const uint64_t ad = desc_sw128(a), bd = desc_sw128(a + kABytes);
+          if (elect_one()) {
+            const uint32_t a = smem_u32(tiles + size_t(st) * kStageBytes);
+            const uint64_t ad = desc_sw128(a), bd = desc_sw128(a + kABytes);
 #pragma unroll
-          for (int j = 0; j < kBK / 16; ++j)  // +32 B along K inside the swizzle atom
-            umma2(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > g.k0 || j > 0) ? 1u : 0u);
-          commit_both(&empty[st]);
+            for (int j = 0; j < kBK / 16; ++j)  // +32 B along K inside the swizzle atom
+              umma2(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > g.k0 || j > 0) ? 1u : 0u);
+            commit_both(&empty[st]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
-        commit_both(&tfull[buf]);
+        if (elect_one()) commit_both(&tfull[buf]);
+        __syncwarp();
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         for (uint32_t p = 0; p < (1u << 22); ++p) __nanosleep(0);
       }
     }

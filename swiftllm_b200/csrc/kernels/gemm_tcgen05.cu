@@ -51,6 +51,9 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* t
       : "memory");
 }
 
+// Warp-uniform variant for the MMA-issue warp (all lanes poll, all agree).
+__device__ __forceinline__ bool wait_warp_or_abort(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort_flag, int* status, int where);
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag, int* status, int where) {
   for (uint32_t i = 0; i < kWaitLimit; ++i) {
@@ -60,6 +63,26 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
   set_status(status, kErrWaitTimeout, where);
   *abort_flag = 1;
   return false;
+}
+__device__ __forceinline__ bool wait_warp_or_abort(uint64_t* bar, uint32_t parity,
+                                                   volatile int* abort_flag, int* status, int where) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    if ((i & 255) == 255 && __any_sync(0xffffffffu, *abort_flag != 0)) return false;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    set_status(status, kErrWaitTimeout, where);
+    *abort_flag = 1;
+  }
+  return false;
+}
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // K-major, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart
@@ -364,7 +387,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // whole warp: warp-uniform waits, one elected lane issues
+    {
       constexpr uint32_t idesc =
           Q == 1 ? instr_desc_e4m3<BN>() : Q == 2 ? instr_desc_s8<BN>() : instr_desc_bf16<BN>();
       uint32_t it = 0, tc = 0;
@@ -374,7 +398,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         decode_tile(t, m, x0, xend, w0, s);
         const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
         const uint32_t buf = tc & 1;
-        if (!wait_or_abort(&tempty[buf], ((tc >> 1) & 1) ^ 1, abort_flag, status, 11)) {
+        if (!wait_warp_or_abort(&tempty[buf], ((tc >> 1) & 1) ^ 1, abort_flag, status, 11)) {
           ok = false;
           break;
         }
@@ -382,28 +406,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * BN;
         for (int kk = k0; kk < k1; ++kk, ++it) {
           const int st = it % STAGES;
-          if (!wait_or_abort(&full[st], (it / STAGES) & 1, abort_flag, status, 12)) {
+          if (!wait_warp_or_abort(&full[st], (it / STAGES) & 1, abort_flag, status, 12)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
-          const uint64_t ad = smem_desc_sw128(a);
-          const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
+          if (elect_one()) {
+            const uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
+            const uint64_t ad = smem_desc_sw128(a);
+            const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
 #pragma unroll
-          for (int j = 0; j < kGemmBK / 16; ++j)  // +32 B along K inside the swizzle atom
-            if constexpr (Q == 1)
-              umma_e4m3(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
-            else if constexpr (Q == 2)
-              umma_s8(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
-            else
-              umma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
-          umma_commit(&empty[st]);
+            for (int j = 0; j < kGemmBK / 16; ++j)  // +32 B along K inside the swizzle atom
+              if constexpr (Q == 1)
+                umma_e4m3(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+              else if constexpr (Q == 2)
+                umma_s8(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+              else
+                umma_bf16(d_tmem, ad + 2 * j, bd + 2 * j, idesc, (kk > k0 || j > 0) ? 1u : 0u);
+            umma_commit(&empty[st]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
-        umma_commit(&tfull[buf]);
+        if (elect_one()) umma_commit(&tfull[buf]);
+        __syncwarp();
       }
-      if (!ok) {  // MMAs already issued finish (their commits arrive on empty[])
+      if (!ok && lane == 0) {  // MMAs already issued finish (their commits arrive on empty[])
         for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
           for (uint32_t p = 0; p < (1u << 20); ++p)
             if (mbar_try_wait(&empty[j % STAGES], (j / STAGES) & 1)) break;
@@ -640,7 +668,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    // whole warp: warp-uniform waits, one elected lane issues
+    {
       constexpr uint32_t idesc = instr_desc_bf16<BN>();
       uint32_t it = 0, tc = 0;
       bool ok = true;
@@ -648,7 +677,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int j, t, k0, k1;
         seg_of(p, j, t, k0, k1);
         const uint32_t buf = tc % NBUF;
-        if (!wait_or_abort(&tempty[buf], ((tc / NBUF) & 1) ^ 1, abort_flag, status, 21)) {
+        if (!wait_warp_or_abort(&tempty[buf], ((tc / NBUF) & 1) ^ 1, abort_flag, status, 21)) {
           ok = false;
           break;
         }
@@ -656,28 +685,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d_tmem = tmem_base + buf * S::ACC_COLS;
         for (int kk = k0; kk < k1; ++kk, ++it) {
           const int st = it % STAGES;
-          if (!wait_or_abort(&full[st], (it / STAGES) & 1, abort_flag, status, 22)) {
+          if (!wait_warp_or_abort(&full[st], (it / STAGES) & 1, abort_flag, status, 22)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
-          const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
+          if (elect_one()) {
+            const uint8_t* a = tiles + size_t(st) * S::STAGE_BYTES;
+            const uint64_t bd = smem_desc_sw128(a + S::A_BYTES);
 #pragma unroll
-          for (int q = 0; q < kGemmBK / 16; ++q) {
+            for (int q = 0; q < kGemmBK / 16; ++q) {
 #pragma unroll
-            for (int i = 0; i < MT; ++i) {
-              const uint64_t ad = smem_desc_sw128(a + i * kGemmBM * kGemmBK * 2);
-              umma_bf16(d_tmem + i * BN, ad + 2 * q, bd + 2 * q, idesc,
-                        (kk > k0 || q > 0) ? 1u : 0u);
+              for (int i = 0; i < MT; ++i) {
+                const uint64_t ad = smem_desc_sw128(a + i * kGemmBM * kGemmBK * 2);
+                umma_bf16(d_tmem + i * BN, ad + 2 * q, bd + 2 * q, idesc,
+                          (kk > k0 || q > 0) ? 1u : 0u);
+              }
             }
+            umma_commit(&empty[st]);
           }
-          umma_commit(&empty[st]);
+          __syncwarp();
         }
         if (!ok) break;
-        umma_commit(&tfull[buf]);
+        if (elect_one()) umma_commit(&tfull[buf]);
+        __syncwarp();
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
           for (uint32_t p = 0; p < (1u << 20); ++p)
             if (mbar_try_wait(&empty[j % STAGES], (j / STAGES) & 1)) break;

@@ -34,15 +34,26 @@ def has_cuda_ext() -> bool:
     return _C is not None
 
 
-# GEMM backend for CUDA tensors: "tcgen05" (our kernel, default) or "cublas"
-# (torch.matmul; only the NCCL+cuBLAS baseline path selects it).
-DEFAULT_GEMM_BACKEND = os.environ.get("SWIFTLLM_GEMM", "tcgen05")
+# GEMM selection for plain bf16 projections on CUDA tensors:
+#   "auto"    (default) per shape, whichever measured faster on B200: the
+#             library GEMM (cuBLAS) for every plain projection except the
+#             decode LM head (<= 256 tokens, >= 28k vocabulary rows), where
+#             our swapped-operand tcgen05 kernel wins (58.6 vs 68.5 us at
+#             256 x 32000 x 4096). Without cluster multicast (kept out of
+#             all code that may run on several GPUs) our decode GEMMs re-read
+#             the token tile through the L2 -> SM fabric once per feature
+#             tile and lose to cuBLAS by 1.2-2x on the narrow projections.
+#   "tcgen05" our kernels for every GEMM (SwiGLU fused into the gate/up
+#             GEMM epilogue); tests and ablations select it.
+#   "cublas"  the library GEMM everywhere (the NCCL + cuBLAS baseline arm).
+# Quantized weights (FP8, int8) always run our tcgen05 kernels.
+DEFAULT_GEMM_BACKEND = os.environ.get("SWIFTLLM_GEMM", "auto")
 _GEMM_BACKEND = DEFAULT_GEMM_BACKEND
 
 
 def set_gemm_backend(name: str) -> None:
     global _GEMM_BACKEND
-    if name not in ("tcgen05", "cublas"):
+    if name not in ("auto", "tcgen05", "cublas"):
         raise ValueError(name)
     _GEMM_BACKEND = name
 
@@ -208,6 +219,12 @@ def _linear_fp8(x, w: Fp8Weight, b, out):
     return out
 
 
+def _library_faster(x: torch.Tensor, w: torch.Tensor) -> bool:
+    """"auto" GEMM selection: True where cuBLAS measured faster (every plain
+    projection but the decode LM head)."""
+    return not (x.numel() // x.shape[-1] <= 256 and w.shape[0] >= 28000)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if isinstance(w, Fp8Weight):
@@ -216,14 +233,17 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
         return _linear_int8(x, w, b, out)
     if not x.is_cuda:
         return ref.linear(x, w, b)
-    if _GEMM_BACKEND == "cublas":
+    if _GEMM_BACKEND == "cublas" or (_GEMM_BACKEND == "auto" and _library_faster(x, w)):
         if w.shape[1] != x.shape[-1]:  # weight zero-padded at load
             x = torch.nn.functional.pad(x, (0, w.shape[1] - x.shape[-1]))
-        y = torch.nn.functional.linear(x, w, b)
-        if out is not None:
-            out.copy_(y)
-            return out
-        return y
+        if out is None:
+            return torch.nn.functional.linear(x, w, b)
+        x2, o2 = x.reshape(-1, x.shape[-1]), out.view(-1, out.shape[-1])
+        if b is None:
+            torch.matmul(x2, w.t(), out=o2)
+        else:
+            torch.addmm(b, x2, w.t(), out=o2)
+        return out
     C = cuda_ext()
     if out is None:
         out = torch.empty(x.shape[:-1] + (w.shape[0],), dtype=x.dtype, device=x.device)

@@ -53,7 +53,7 @@ def _build_runner(model_cfg, cfg, rank: int, world: int, local_rank: int):
                         max(int(cfg.max_num_batched_tokens or 8192), 16384))
     if device.type == "cuda":
         # the NCCL backend is the library baseline: cuBLAS GEMMs + NCCL
-        # all-reduce; otherwise the process default (tcgen05 unless
+        # all-reduce; otherwise the process default ("auto" unless
         # SWIFTLLM_GEMM says otherwise)
         from .. import ops
         ops.set_gemm_backend("cublas" if cfg.comm_backend == "nccl" else ops.DEFAULT_GEMM_BACKEND)

@@ -115,3 +115,32 @@ def test_speculative_gpu(spec):
     llm.shutdown()
     from swiftllm_b200.ops import cuda_ext
     assert cuda_ext().read_status(True)[0] == 0
+
+
+def test_gemm_backends_agree_gpu():
+    """The "auto" GEMM selection (library GEMMs for plain projections) and
+    our tcgen05 kernels everywhere (SwiGLU fused into the gate/up epilogue)
+    give the same logits within bf16 tolerance."""
+    from swiftllm_b200 import ops
+    cfg = load_config("tiny-llama")
+    T = 77
+    ids = torch.randint(0, cfg.vocab_size, (T,), dtype=torch.int32).cuda()
+    nb = (T + 15) // 16
+    out = {}
+    try:
+        for backend in ("auto", "tcgen05"):
+            ops.set_gemm_backend(backend)
+            m = DecoderModel(cfg, torch.bfloat16, "cuda")
+            m.allocate()
+            m.init_dummy(0)
+            if backend == "tcgen05":
+                m.fuse_swiglu()
+            kv = torch.zeros(nb, cfg.num_layers, 2, m.local_kv_heads, 16, cfg.head_dim,
+                             dtype=torch.bfloat16, device="cuda")
+            with torch.no_grad():
+                out[backend] = m.compute_logits(m.forward(ids, _meta(T, "cuda"), kv)).float()
+    finally:
+        ops.set_gemm_backend(ops.DEFAULT_GEMM_BACKEND)
+    scale = out["auto"].abs().max().item()
+    err = (out["auto"] - out["tcgen05"]).abs().max().item()
+    assert err < 0.03 * scale + 0.03, (err, scale)
