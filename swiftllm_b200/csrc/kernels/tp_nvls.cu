@@ -36,6 +36,8 @@
 // passed arrival 2, which every rank makes only after reading `in`; `out` is
 // written only after arrival 1, which a rank makes only after its consumer
 // of the previous `out` (the GEMM before this kernel) has finished.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace swift {
@@ -115,7 +117,9 @@ __device__ __forceinline__ bool rn_barrier(const RnPeers& P, int rank, int k, in
   __syncthreads();
   if (threadIdx.x == 0) {
     ok = 1;
-    __threadfence_system();
+    // no separate fence: the block's stores are ordered before thread 0 by
+    // the barrier above, and the release of the arrival is cumulative over
+    // them (release at system scope covers the peers' view of them)
     const int64_t off = ctr_off + int64_t(blockIdx.x) * 4;
     if constexpr (MC) {
       mc_red_release(P.mc + off, 1u);
@@ -263,12 +267,17 @@ int64_t tp_reduce_norm(std::vector<int64_t> bases, int64_t mc, int64_t rank, int
   }
   const int64_t tns = static_cast<int64_t>(timeout_s * 1e9);
   auto ep = reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>());
+  // one block per owned row up to kRnBlocks: a block takes part in both
+  // cross-rank barriers whether or not it owns rows, so idle blocks only add
+  // arrivals. Every rank computes the same grid from (T, k), and block b's
+  // counter and epoch advance only when block b runs, on every rank alike.
+  const int blocks = static_cast<int>(std::min<int64_t>(kRnBlocks, std::max<int64_t>(1, (T + k - 1) / k)));
   if (P.mc)
-    launch_pdl(tp_reduce_norm_kernel<true>, dim3(kRnBlocks), dim3(kRnThreads), 0, cur_stream(), 
+    launch_pdl(tp_reduce_norm_kernel<true>, dim3(blocks), dim3(kRnThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, in_off, out_off, ctr_off, rp, wp, static_cast<float>(eps),
         static_cast<int>(T), static_cast<int>(H), ep, tns, status_word_ptr());
   else
-    launch_pdl(tp_reduce_norm_kernel<false>, dim3(kRnBlocks), dim3(kRnThreads), 0, cur_stream(), 
+    launch_pdl(tp_reduce_norm_kernel<false>, dim3(blocks), dim3(kRnThreads), 0, cur_stream(), 
         P, static_cast<int>(rank), k, in_off, out_off, ctr_off, rp, wp, static_cast<float>(eps),
         static_cast<int>(T), static_cast<int>(H), ep, tns, status_word_ptr());
   SWIFT_CHECK_LAUNCH();
