@@ -283,6 +283,9 @@ PYBIND11_MODULE(_core, m) {
            py::arg("batch"), py::arg("tokens"), py::arg("counts"), py::arg("logprobs") = py::none(),
            py::arg("now") = 0.0)
       .def("decode_ready_seqs", [](const Scheduler& s) { return to_np(s.decode_ready_seqs()); })
+      .def("beam_update", &Scheduler::beam_update, py::arg("group"), py::arg("live_parent"),
+           py::arg("live_token"), py::arg("live_logprob"), py::arg("fin_parent"), py::arg("fin_token"),
+           py::arg("fin_logprob"), py::arg("now") = 0.0)
       .def("append_tokens", &Scheduler::append_tokens)
       .def("rollback", &Scheduler::rollback)
       .def_property_readonly("num_waiting", &Scheduler::num_waiting)

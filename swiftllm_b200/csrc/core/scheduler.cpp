@@ -498,6 +498,8 @@ StepResult Scheduler::update_multi(const Batch& b, const int32_t* tokens, const 
     if (sit == seqs_.end()) continue;
     Sequence& s = sit->second;
     if (s.status != SeqStatus::RUNNING) continue;  // aborted meanwhile
+    // a negative token marks a row the caller handles itself (beam search)
+    if (first[r + 1] > first[r] && tokens[first[r]] < 0) continue;
     const GroupParams& p = g.params;
     for (int64_t q = first[r]; q < first[r + 1]; ++q) {
       int32_t tok = tokens[q];
@@ -535,6 +537,105 @@ StepResult Scheduler::update_multi(const Batch& b, const int32_t* tokens, const 
   std::sort(touched.begin(), touched.end());
   touched.erase(std::unique(touched.begin(), touched.end()), touched.end());
   for (int64_t gid : touched) finish_group_if_done(gid, now, &res);
+  return res;
+}
+
+StepResult Scheduler::beam_update(int64_t gid, const std::vector<int64_t>& live_parent,
+                                  const std::vector<int32_t>& live_token,
+                                  const std::vector<float>& live_logprob,
+                                  const std::vector<int64_t>& fin_parent,
+                                  const std::vector<int32_t>& fin_token,
+                                  const std::vector<float>& fin_logprob, double now) {
+  StepResult res;
+  if (live_parent.size() != live_token.size() || live_parent.size() != live_logprob.size() ||
+      fin_parent.size() != fin_token.size() || fin_parent.size() != fin_logprob.size())
+    throw std::invalid_argument("beam_update: mismatched candidate arrays");
+  auto git = groups_.find(gid);
+  if (git == groups_.end()) return res;
+  Group& g = git->second;
+  for (int64_t p : live_parent)
+    if (std::find(g.seqs.begin(), g.seqs.end(), p) == g.seqs.end() || seqs_.at(p).status != SeqStatus::RUNNING)
+      throw std::invalid_argument("beam_update: parent is not a running beam of the group");
+  for (int64_t p : fin_parent)
+    if (std::find(g.seqs.begin(), g.seqs.end(), p) == g.seqs.end() || seqs_.at(p).status != SeqStatus::RUNNING)
+      throw std::invalid_argument("beam_update: parent is not a running beam of the group");
+  if (g.first_token < 0) g.first_token = now;
+  auto record = [&](int64_t sid, int32_t tok) {
+    res.group.push_back(gid);
+    res.seq.push_back(sid);
+    res.token.push_back(tok);
+    res.row.push_back(-1);
+  };
+  // finished hypotheses: copies of the parent's tokens plus the final token
+  for (size_t j = 0; j < fin_parent.size(); ++j) {
+    const Sequence& ps = seqs_.at(fin_parent[j]);
+    Sequence c;
+    c.id = next_seq_++;
+    c.group = gid;
+    c.tokens = ps.tokens;
+    c.tokens.push_back(fin_token[j]);
+    c.num_prompt = ps.num_prompt;
+    c.num_computed = 0;
+    c.cum_logprob = ps.cum_logprob + fin_logprob[j];
+    c.status = SeqStatus::FINISHED_STOPPED;
+    record(c.id, fin_token[j]);
+    g.seqs.push_back(c.id);
+    seqs_.emplace(c.id, std::move(c));
+  }
+  // live beams: forks first (they copy the parent before it appends)
+  std::vector<int64_t> target(live_parent.size(), -1);
+  std::vector<int64_t> claimed;
+  for (size_t j = 0; j < live_parent.size(); ++j) {
+    const int64_t p = live_parent[j];
+    if (std::find(claimed.begin(), claimed.end(), p) == claimed.end()) {
+      claimed.push_back(p);
+      target[j] = p;
+    }
+  }
+  for (size_t j = 0; j < live_parent.size(); ++j) {
+    if (target[j] >= 0) continue;
+    const Sequence& ps = seqs_.at(live_parent[j]);
+    Sequence c;
+    c.id = next_seq_++;
+    c.group = gid;
+    c.tokens = ps.tokens;
+    c.num_prompt = ps.num_prompt;
+    c.num_computed = ps.num_computed;
+    c.cum_logprob = ps.cum_logprob;
+    c.status = SeqStatus::RUNNING;
+    bm_->fork(ps.id, c.id);
+    target[j] = c.id;
+    g.seqs.push_back(c.id);
+    seqs_.emplace(c.id, std::move(c));
+  }
+  // running beams that no live child continues leave the group
+  std::vector<int64_t> keep;
+  for (int64_t sid : g.seqs) {
+    Sequence& s = seqs_.at(sid);
+    const bool old_live = s.status == SeqStatus::RUNNING &&
+                          std::find(target.begin(), target.end(), sid) == target.end();
+    if (old_live) {
+      free_seq(s);
+      seqs_.erase(sid);
+    } else {
+      keep.push_back(sid);
+    }
+  }
+  g.seqs = keep;
+  const GroupParams& p = g.params;
+  for (size_t j = 0; j < live_parent.size(); ++j) {
+    Sequence& s = seqs_.at(target[j]);
+    s.tokens.push_back(live_token[j]);
+    s.cum_logprob += live_logprob[j];
+    record(s.id, live_token[j]);
+    if (s.num_output() >= p.max_tokens || static_cast<int64_t>(s.tokens.size()) >= cfg_.max_model_len) {
+      free_seq(s);
+      s.status = SeqStatus::FINISHED_LENGTH;
+    } else {
+      s.num_computed = static_cast<int64_t>(s.tokens.size()) - 1;
+    }
+  }
+  finish_group_if_done(gid, now, &res);
   return res;
 }
 

@@ -174,6 +174,22 @@ class Scheduler {
   // running sequences whose next step is a plain decode (one token to compute)
   std::vector<int64_t> decode_ready_seqs() const;
 
+  // Beam search (SamplingParams.use_beam_search; the reference's
+  // BeamSearchSampler, crates/swiftllm-core/src/sampling/strategies.rs:
+  // 295-357, only keeps the top candidates of one sequence). The caller has
+  // ranked the candidates of group `gid` and passes the next step's live
+  // beams and the newly finished hypotheses as (parent sequence, token,
+  // token logprob). A parent's first live child continues it in place,
+  // further children are forks sharing its KV blocks (copy-on-write on
+  // append); live beams no child continues are dropped from the group and
+  // their blocks freed; a finished hypothesis becomes a finished sequence of
+  // the group that holds no blocks. Beams reaching max_tokens or the model
+  // length finish with FINISHED_LENGTH.
+  StepResult beam_update(int64_t gid, const std::vector<int64_t>& live_parent,
+                         const std::vector<int32_t>& live_token, const std::vector<float>& live_logprob,
+                         const std::vector<int64_t>& fin_parent, const std::vector<int32_t>& fin_token,
+                         const std::vector<float>& fin_logprob, double now);
+
   int num_waiting() const { return static_cast<int>(waiting_.size()); }
   int num_running() const { return static_cast<int>(running_.size()); }
   int num_swapped() const { return static_cast<int>(swapped_.size()); }

@@ -44,6 +44,7 @@ class _Req:
     finished_seqs: Dict[int, str] = field(default_factory=dict)
     done: bool = False
     arrival: float = 0.0
+    beam_fin: List[Any] = field(default_factory=list)  # (penalised score, seq) of finished hypotheses
 
 
 def prepare_config(c: EngineConfig):
@@ -152,10 +153,12 @@ class LLMEngine:
             if prompt is None:
                 raise ValueError("either prompt or prompt_token_ids is required")
             prompt_token_ids = list(self.tokenizer.encode(prompt))
-        if sp.use_beam_search:
-            raise NotImplementedError("beam search is not supported; use n/best_of sampling")
+        if sp.use_beam_search and sp.logprobs is not None:
+            raise ValueError("beam search does not return per-token logprobs")
         gp = _core.GroupParams()
-        gp.n = max(sp.n, sp.best_of)
+        # beam search: one sequence at admission; the beams are forked by
+        # the engine's beam step (width max(n, best_of))
+        gp.n = 1 if sp.use_beam_search else max(sp.n, sp.best_of)
         gp.max_tokens = sp.max_tokens
         gp.min_tokens = sp.min_tokens
         gp.ignore_eos = sp.ignore_eos
@@ -254,8 +257,9 @@ class LLMEngine:
         from ..runtime.model_runner import step_input_from_batch
         si = step_input_from_batch(b)
         want_lp_rows = self._wants_logprobs(b) if b.num_sample_rows else False
+        beam_rows = self._beam_rows(b) if b.num_sample_rows else {}
         if self.config.tensor_parallel_size > 1 and b.num_sample_rows and not b.any_penalty \
-                and not want_lp_rows:
+                and not want_lp_rows and not beam_rows:
             temp = np.asarray(b.temperature)
             si.greedy = bool(np.all((temp <= 0.0) | (np.asarray(b.top_k) == 1)))
         logits = self.executor.execute(si)
@@ -269,10 +273,109 @@ class LLMEngine:
         with nvtx.range("sample"):
             toks, lps = self.sampler(logits, b, self._history)
         want_lp = self._top_logprobs(logits, b, toks) if want_lp_rows else None
+        if beam_rows:
+            toks = np.array(toks, dtype=np.int32, copy=True)
+            for rows in beam_rows.values():
+                toks[rows] = -1  # handled by the beam step below
         res = self.scheduler.update(b, toks, lps, time.monotonic())
-        self._gen_tokens += len(res.token)
-        self._account(si, b, len(res.token))
-        return outs + self._process(res, want_lp)
+        ntok = len(res.token)
+        outs += self._process(res, want_lp)
+        if beam_rows:
+            with nvtx.range("beam"):
+                for gid, rows in beam_rows.items():
+                    o, n = self._beam_step(gid, rows, logits, b)
+                    outs += o
+                    ntok += n
+        self._gen_tokens += ntok
+        self._account(si, b, ntok)
+        return outs
+
+    # ------------------------------------------------------------ beam search
+    def _beam_rows(self, b) -> Dict[int, List[int]]:
+        """Sample rows of beam-search groups in this batch, by group."""
+        out: Dict[int, List[int]] = {}
+        for i, g in enumerate(np.asarray(b.sample_group).tolist()):
+            r = self._by_gid.get(int(g))
+            if r is not None and r.params.use_beam_search:
+                out.setdefault(int(g), []).append(i)
+        return out
+
+    @staticmethod
+    def _beam_score(cum: float, n_out: int, length_penalty: float) -> float:
+        return cum / (max(n_out, 1) ** length_penalty)
+
+    def _beam_step(self, gid: int, rows: List[int], logits, b):
+        """One beam-search step for group ``gid`` (its beams are ``rows`` of
+        the batch): every beam proposes its 2W best next tokens, candidates
+        are ranked by cumulative log-probability, the first W that do not end
+        the sequence become the live beams, ending candidates ranked among
+        the first W become finished hypotheses (scored cum / len^length_penalty).
+        The group stops when no beam is live, or (early_stopping) once W
+        hypotheses are finished, or when no live beam can still beat the
+        worst of the W best finished ones. Returns (outputs, tokens appended)."""
+        import torch
+        r = self._by_gid[gid]
+        sp = r.params
+        W = max(sp.n, sp.best_of)
+        lidx = torch.as_tensor([int(b.sample_logit_idx[i]) for i in rows], dtype=torch.long,
+                               device=logits.device)
+        lp = torch.log_softmax(logits.index_select(0, lidx).float(), dim=-1)
+        kk = min(2 * W, lp.shape[-1])
+        tv, ti = lp.topk(kk, dim=-1)
+        tv, ti = tv.cpu().numpy(), ti.cpu().numpy()
+        sids = [int(b.sample_target_seq[i]) for i in rows]
+        info = {sid: self.scheduler.seq_info(sid) for sid in sids}
+        eos = self.eos_token_id if not sp.ignore_eos else None
+        stops = set(sp.stop_token_ids or [])
+        cands = []
+        for j, sid in enumerate(sids):
+            cum = float(info[sid]["cum_logprob"])
+            for q in range(kk):
+                cands.append((cum + float(tv[j, q]), sid, int(ti[j, q]), float(tv[j, q])))
+        cands.sort(key=lambda c: -c[0])
+        live, fin = [], []
+        for rank, (score, sid, tok, v) in enumerate(cands):
+            n_out = int(info[sid]["num_output"]) + 1
+            ends = n_out > sp.min_tokens and ((eos is not None and tok == eos) or tok in stops)
+            if ends:
+                if rank < W:
+                    fin.append((sid, tok, v, n_out, score))
+            elif len(live) < W:
+                live.append((sid, tok, v))
+            if len(live) == W:
+                break
+        res = self.scheduler.beam_update(gid, [c[0] for c in live], [c[1] for c in live],
+                                         [c[2] for c in live], [c[0] for c in fin],
+                                         [c[1] for c in fin], [c[2] for c in fin], time.monotonic())
+        new_seqs = np.asarray(res.seq).tolist()
+        for k, c in enumerate(fin):
+            r.beam_fin.append((self._beam_score(c[4], c[3], sp.length_penalty), new_seqs[k]))
+        r.beam_fin.sort(key=lambda x: -x[0])
+        del r.beam_fin[W:]
+        # stopping rules
+        info_g = self.scheduler.group_info(gid)
+        live_now = [s for s in (info_g["seqs"] if info_g else [])
+                    if self.scheduler.seq_info(s)["status"] == "running"]
+        stop = False
+        if live_now and len(r.beam_fin) >= W:
+            if sp.early_stopping:
+                stop = True
+            else:
+                best_live = max(float(self.scheduler.seq_info(s)["cum_logprob"]) for s in live_now)
+                n_out = max(int(self.scheduler.seq_info(s)["num_output"]) for s in live_now)
+                stop = self._beam_score(best_live, n_out, sp.length_penalty) <= r.beam_fin[-1][0]
+        if stop:
+            for s in live_now:
+                self.scheduler.finish_seq(s, "abort")
+        info_g = self.scheduler.group_info(gid)
+        done = info_g is None or all(self.scheduler.seq_info(s)["status"] not in
+                                     ("running", "waiting", "swapped") for s in info_g["seqs"])
+        outs = []
+        if done and not r.done:
+            outs.append(self._final_output(r))
+        elif r.stream:
+            outs.append(self._make_output(r, final=False))
+        return outs, len(res.token)
 
     def _rejected(self, b) -> List[RequestOutput]:
         outs = []
@@ -389,7 +492,18 @@ class LLMEngine:
                 cumulative_logprob=float(si["cum_logprob"]),
                 logprobs=r.logprobs.get(sid), finish_reason=fr if final or fr else None,
                 stop_reason=stop_reason))
-        if final and r.params.best_of > r.params.n and len(comps) > r.params.n:
+        if r.params.use_beam_search:
+            # beams: the best finished hypotheses (and beams cut by the
+            # length limit) by length-penalised score; beams stopped early
+            # or dropped are not results
+            lp = r.params.length_penalty
+            comps = [c for c in comps if c.finish_reason != FinishReason.ABORT or aborted]
+            comps.sort(key=lambda c: -self._beam_score(c.cumulative_logprob or 0.0,
+                                                        len(c.token_ids), lp))
+            comps = comps[: r.params.n]
+            for i, c in enumerate(comps):
+                c.index = i
+        elif final and r.params.best_of > r.params.n and len(comps) > r.params.n:
             comps.sort(key=lambda c: -(c.cumulative_logprob or 0.0))
             comps = comps[: r.params.n]
             for i, c in enumerate(comps):
