@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3)
                         int64_t layer_off, int64_t kv_stride, const int32_t* __restrict__ bt,
                         int64_t bt_stride, const int32_t* __restrict__ seq_lens, int Hq, int Hkv,
                         int splits, float scale, int window, float* __restrict__ ws,
-                        int* status) {
+                        int* status, const float* __restrict__ alibi) {
   using C = DecodeCfg<D, BS>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
@@ -153,7 +153,9 @@ __global__ void __launch_bounds__(kDecWarps * 32, 3)
       if (g < G) {
 #pragma unroll
         for (int o = C::LPT / 2; o > 0; o >>= 1) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
-        s[g] = valid ? s[g] * scale : -INFINITY;
+        // ALiBi: + slope(head) * (key position - query position)
+        const float bias = alibi != nullptr ? alibi[kvh * G + g] * float(t_abs - (len - 1)) : 0.f;
+        s[g] = valid ? s[g] * scale + bias : -INFINITY;
         float pm = warp_max(s[g]);
         float mn = fmaxf(m[g], pm);
         float corr = mn == -INFINITY ? 1.f : __expf(m[g] - mn);
@@ -281,7 +283,7 @@ __global__ void decode_combine_kernel(__nv_bfloat16* __restrict__ out, const flo
 template <int D, int BS>
 static void launch_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                           torch::Tensor bt, torch::Tensor seq_lens, int rows, int splits,
-                          double scale, int window, torch::Tensor ws) {
+                          double scale, int window, torch::Tensor ws, const float* alibi) {
   using C = DecodeCfg<D, BS>;
   const int Hq = static_cast<int>(q.size(1)), Hkv = static_cast<int>(kv.size(3));
   TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= kMaxGroup, "GQA group must be <= 8");
@@ -304,7 +306,7 @@ static void launch_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, 
       reinterpret_cast<const __nv_bfloat16*>(kv.data_ptr<at::BFloat16>()), kv.stride(0),
       layer * kv.stride(1), kv.stride(2), bt.data_ptr<int32_t>(), bt.stride(0),
       seq_lens.data_ptr<int32_t>(), Hq, Hkv, splits, static_cast<float>(scale), window,
-      splits > 1 ? ws.data_ptr<float>() : nullptr, status_word_ptr());
+      splits > 1 ? ws.data_ptr<float>() : nullptr, status_word_ptr(), alibi);
   SWIFT_CHECK_LAUNCH();
   if (splits > 1) {
     decode_combine_kernel<D><<<dim3(rows, Hq), 128, 0, st>>>(
@@ -317,9 +319,12 @@ static void launch_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, 
 // out, q: [T, Hq, D] (the first `rows` rows are decode rows); kv pool
 // [blocks, layers, 2, Hkv, BS, D]; bt [S, max_blocks]; seq_lens [S].
 // Returns the number of kernels launched.
+// alibi: optional fp32 [Hq] ALiBi slopes (then the CUDA-core kernel runs;
+// the tensor-core kernel has no bias term).
 int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                      torch::Tensor bt, torch::Tensor seq_lens, int64_t rows, int64_t splits,
-                     double scale, int64_t window, torch::Tensor ws) {
+                     double scale, int64_t window, torch::Tensor ws,
+                     c10::optional<torch::Tensor> alibi) {
   CHECK_BF16(q);
   CHECK_BF16(kv);
   CHECK_CONTIG(kv);
@@ -331,8 +336,15 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
   splits = std::max<int64_t>(1, splits);
   if (splits > 1)
     TORCH_CHECK(ws.numel() >= rows * q.size(1) * splits * (D + 2), "decode workspace too small");
+  const float* ap = nullptr;
+  if (alibi.has_value()) {
+    TORCH_CHECK(alibi->scalar_type() == at::kFloat && alibi->is_contiguous() &&
+                    alibi->numel() == q.size(1) && alibi->is_cuda(),
+                "paged_decode: alibi slopes must be fp32 [num_heads] on the device");
+    ap = alibi->data_ptr<float>();
+  }
   // tensor-core path (block size 16, head_dim 64 / 128)
-  if (paged_decode_tc(out, q, kv, layer, bt, seq_lens, static_cast<int>(rows),
+  if (ap == nullptr && paged_decode_tc(out, q, kv, layer, bt, seq_lens, static_cast<int>(rows),
                       static_cast<int>(splits), scale, static_cast<int>(window), ws)) {
     if (splits == 1) return 1;
     const int Hq = static_cast<int>(q.size(1));
@@ -351,7 +363,7 @@ int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64
 #define DEC_CASE(d, bs)                                                                  \
   if (D == d && BS == bs) {                                                              \
     launch_decode<d, bs>(out, q, kv, layer, bt, seq_lens, static_cast<int>(rows),         \
-                         static_cast<int>(splits), scale, static_cast<int>(window), ws); \
+                         static_cast<int>(splits), scale, static_cast<int>(window), ws, ap); \
     return splits > 1 ? 2 : 1;                                                           \
   }
   DEC_CASE(128, 16)
@@ -429,7 +441,7 @@ int noalloc_decode(void* out, const void* q, const void* kv, int64_t blk_stride,
   kern<<<grid, kDecWarps * 32, C::smem_for(Hq / Hkv), stream>>>(
       static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
       static_cast<const __nv_bfloat16*>(kv), blk_stride, layer_off, kv_stride, bt, bt_stride,
-      seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, status);
+      seq_lens, Hq, Hkv, splits, scale, window, splits > 1 ? scratch : nullptr, status, nullptr);
   if (cudaGetLastError() != cudaSuccess) return SWIFT_NOALLOC_ERR_CUDA;
   if (splits > 1) {
     decode_combine_kernel<D><<<dim3(rows, Hq), 128, 0, stream>>>(

@@ -58,7 +58,8 @@ __global__ void __launch_bounds__(kPfWarps * 32)
                          int64_t layer_off, int64_t kv_stride, int block_size,
                          const int32_t* __restrict__ bt, int64_t bt_stride,
                          const int32_t* __restrict__ q_start, const int32_t* __restrict__ seq_lens,
-                         int seq0, int Hq, int Hkv, float scale, int window) {
+                         int seq0, int Hq, int Hkv, float scale, int window,
+                         const float* __restrict__ alibi) {
   constexpr int LD = D + 8;   // padded row (elements)
   constexpr int NKT = D / 16; // k-steps over head_dim
   constexpr int NDT = D / 8;  // n-tiles over head_dim
@@ -116,6 +117,8 @@ __global__ void __launch_bounds__(kPfWarps * 32)
   float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
   uint32_t qf[NKT][4];
   const float sl2 = scale * 1.4426950408889634f;  // exp(x) = exp2(x * log2 e)
+  // ALiBi slope of this head in the exp2 domain (0: no bias)
+  const float ab2 = alibi != nullptr ? alibi[head] * 1.4426950408889634f : 0.f;
 
   for (int kb = kb_begin; kb < kb_end; ++kb) {
     const int buf = (kb - kb_begin) & 1;
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(kPfWarps * 32)
       for (int e = 0; e < 4; ++e) {
         int key = kb * kPfBN + n * 8 + (lane & 3) * 2 + (e & 1);
         int qp = e < 2 ? qposA : qposB;
-        float v = s[n][e] * sl2;
+        float v = s[n][e] * sl2 + ab2 * float(key - qp);
         if (need_mask) {
           bool bad = key > qp || key >= L || (window > 0 && key <= qp - window);
           v = bad ? -INFINITY : v;
@@ -241,7 +244,8 @@ __global__ void __launch_bounds__(kPfWarps * 32)
 template <int D>
 static void launch_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                            torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens,
-                           int seq0, int seq1, int max_q_len, double scale, int window) {
+                           int seq0, int seq1, int max_q_len, double scale, int window,
+                           const float* alibi) {
   static_assert((D / 8) % 2 == 0, "head_dim/8 must be even");
   constexpr int LD = D + 8;
   const size_t smem = size_t(kPfBM + 4 * kPfBN) * LD * 2;
@@ -262,7 +266,7 @@ static void launch_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv,
       reinterpret_cast<const __nv_bfloat16*>(kv.data_ptr<at::BFloat16>()), kv.stride(0),
       layer * kv.stride(1), kv.stride(2), static_cast<int>(kv.size(4)), bt.data_ptr<int32_t>(),
       bt.stride(0), q_start.data_ptr<int32_t>(), seq_lens.data_ptr<int32_t>(), seq0, Hq, Hkv,
-      static_cast<float>(scale), window);
+      static_cast<float>(scale), window, alibi);
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -273,9 +277,11 @@ void paged_prefill_tc(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int6
 
 // impl: -1 the tcgen05 kernel (attention_prefill_tc.cu) where it applies
 // (head_dim 128, 16-token pages), else this one; 0 this one; 1 tcgen05.
+// alibi: optional fp32 [Hq] ALiBi slopes (this kernel only).
 void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                    torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int64_t seq0,
-                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl) {
+                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl,
+                   c10::optional<torch::Tensor> alibi) {
   CHECK_BF16(q);
   CHECK_BF16(kv);
   CHECK_CONTIG(kv);
@@ -286,16 +292,24 @@ void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t
   const int a = static_cast<int>(seq0), b = static_cast<int>(seq1), mq = static_cast<int>(max_q_len);
   const bool tc_ok = paged_prefill_tc_supported(D, static_cast<int>(kv.size(4)),
                                                 static_cast<int>(q.size(1)), static_cast<int>(kv.size(3)));
+  const float* ap = nullptr;
+  if (alibi.has_value()) {
+    TORCH_CHECK(alibi->scalar_type() == at::kFloat && alibi->is_contiguous() &&
+                    alibi->numel() == q.size(1) && alibi->is_cuda(),
+                "paged_prefill: alibi slopes must be fp32 [num_heads] on the device");
+    TORCH_CHECK(impl != 1, "paged_prefill: the tcgen05 kernel has no ALiBi bias");
+    ap = alibi->data_ptr<float>();
+  }
   TORCH_CHECK(impl != 1 || tc_ok, "paged_prefill: the tcgen05 kernel needs head_dim 128 and 16-token pages");
-  if (impl != 0 && tc_ok) {
+  if (impl != 0 && tc_ok && ap == nullptr) {
     paged_prefill_tc(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w);
     return;
   }
   switch (D) {
-    case 64: launch_prefill<64>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;
-    case 80: launch_prefill<80>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;
-    case 96: launch_prefill<96>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;
-    case 128: launch_prefill<128>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w); break;
+    case 64: launch_prefill<64>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w, ap); break;
+    case 80: launch_prefill<80>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w, ap); break;
+    case 96: launch_prefill<96>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w, ap); break;
+    case 128: launch_prefill<128>(out, q, kv, layer, bt, q_start, seq_lens, a, b, mq, scale, w, ap); break;
     default: TORCH_CHECK(false, "paged_prefill: unsupported head_dim ", D);
   }
 }

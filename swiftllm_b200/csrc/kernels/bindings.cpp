@@ -24,10 +24,12 @@ void init_normal(torch::Tensor v, int64_t key, double std, int64_t full_rows, in
 std::vector<int64_t> read_status(bool clear);
 int64_t paged_decode(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                      torch::Tensor bt, torch::Tensor seq_lens, int64_t rows, int64_t splits,
-                     double scale, int64_t window, torch::Tensor ws);
+                     double scale, int64_t window, torch::Tensor ws,
+                     c10::optional<torch::Tensor> alibi);
 void paged_prefill(torch::Tensor out, torch::Tensor q, torch::Tensor kv, int64_t layer,
                    torch::Tensor bt, torch::Tensor q_start, torch::Tensor seq_lens, int64_t seq0,
-                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl);
+                   int64_t seq1, int64_t max_q_len, double scale, int64_t window, int64_t impl,
+                   c10::optional<torch::Tensor> alibi);
 void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch::Tensor fparams,
             torch::Tensor iparams, torch::Tensor keys, bool any_random);
 int64_t gemm(torch::Tensor out, torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> bias);
@@ -77,12 +79,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_blocks", &swift::copy_blocks);
   m.def("init_normal", &swift::init_normal);
   m.def("read_status", &swift::read_status, pybind11::arg("clear") = true);
-  m.def("paged_decode", &swift::paged_decode);
+  m.def("paged_decode", &swift::paged_decode, pybind11::arg("out"), pybind11::arg("q"),
+        pybind11::arg("kv"), pybind11::arg("layer"), pybind11::arg("bt"), pybind11::arg("seq_lens"),
+        pybind11::arg("rows"), pybind11::arg("splits"), pybind11::arg("scale"),
+        pybind11::arg("window"), pybind11::arg("ws"), pybind11::arg("alibi") = pybind11::none());
   m.def("paged_prefill", &swift::paged_prefill, pybind11::arg("out"), pybind11::arg("q"),
         pybind11::arg("kv"), pybind11::arg("layer"), pybind11::arg("bt"), pybind11::arg("q_start"),
         pybind11::arg("seq_lens"), pybind11::arg("seq0"), pybind11::arg("seq1"),
         pybind11::arg("max_q_len"), pybind11::arg("scale"), pybind11::arg("window"),
-        pybind11::arg("impl") = -1);
+        pybind11::arg("impl") = -1, pybind11::arg("alibi") = pybind11::none());
   m.def("sample", &swift::sample);
   m.def("apply_penalties", &swift::apply_penalties);
   m.def("gemm", &swift::gemm);

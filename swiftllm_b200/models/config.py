@@ -50,6 +50,7 @@ class ModelConfig:
     hidden_act: str = "silu"
     norm_type: str = "rmsnorm"         # "rmsnorm" | "layernorm" (Phi)
     parallel_block: bool = False       # Phi: attention and MLP read the same input
+    position_embedding: str = "rope"   # "rope" | "alibi" (per-head linear score bias, no RoPE)
     bos_token_id: int = 1
     eos_token_id: int = 2
     name: str = ""
@@ -76,6 +77,8 @@ class ModelConfig:
 
     @property
     def rotary_dim(self) -> int:
+        if self.position_embedding == "alibi":
+            return 0
         return int(self.head_dim * self.partial_rotary_factor)
 
     def kv_cache_bytes_per_token(self, dtype_bytes: int = 2) -> int:
@@ -99,6 +102,11 @@ PRESETS: Dict[str, ModelConfig] = {
                               num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
                               vocab_size=32000, rms_norm_eps=1e-5, rope_theta=10000.0,
                               max_position_embeddings=2048),
+    # the tiny LLaMA with ALiBi instead of RoPE (kernel / engine coverage)
+    "tiny-llama-alibi": ModelConfig(architecture="llama", hidden_size=256, intermediate_size=688,
+                                    num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
+                                    vocab_size=32000, rms_norm_eps=1e-5, position_embedding="alibi",
+                                    max_position_embeddings=2048),
     "llama-2-7b": ModelConfig(architecture="llama", hidden_size=4096, intermediate_size=11008,
                               num_layers=32, num_heads=32, num_kv_heads=32, head_dim=128,
                               vocab_size=32000, rope_theta=10000.0, max_position_embeddings=4096),

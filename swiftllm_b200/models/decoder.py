@@ -125,6 +125,14 @@ class DecoderModel:
         self.max_pos = max_pos or cfg.max_position_embeddings
         self.cos_sin = cos_sin_table(cfg.rotary_dim, cfg.rope_theta, self.max_pos,
                                      cfg.rope_scaling, device=self.device)
+        # ALiBi (position_embedding="alibi"): this rank's heads' slopes
+        # (Megatron head split: rank r holds heads [r * local, (r + 1) * local))
+        self.alibi = None
+        if cfg.position_embedding == "alibi":
+            from ..ops.reference import alibi_slopes
+            h0 = r * self.local_heads
+            self.alibi = alibi_slopes(cfg.num_heads)[h0:h0 + self.local_heads].float().contiguous().to(
+                self.device)
         self.layers: List[SimpleNamespace] = []
         self.embed = None
         self.norm_w = None
@@ -313,7 +321,7 @@ class DecoderModel:
         q = ops.qkv_rope_cache(qkv, meta.positions, self.cos_sin, kv_cache, i, meta.slot_mapping,
                                self.local_heads, self.local_kv_heads, c.head_dim, c.rotary_dim,
                                L.bqkv)
-        a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
+        a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window, self.alibi)
         a2 = a.reshape(a.shape[0], -1)
         if reduce:  # o_proj + cross-rank sum (one fused GEMM -> reduce-scatter under TP)
             return self.tp.linear_reduce(a2, L.wo)
@@ -362,7 +370,7 @@ class DecoderModel:
             q = ops.qkv_rope_cache(ops.linear(x, L.wqkv), meta.positions, self.cos_sin, kv_cache, i,
                                    meta.slot_mapping, self.local_heads, self.local_kv_heads,
                                    c.head_dim, c.rotary_dim, L.bqkv)
-            a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window)
+            a = ops.attention(q, kv_cache, i, meta, self.scale, c.sliding_window, self.alibi)
             ops.linear(a.reshape(T, -1), L.wo, out=self.tp.reduce_buffer(T, H))
             x = self.tp.reduce_norm(T, h, L.ln2, c.rms_norm_eps)
             if c.num_experts:

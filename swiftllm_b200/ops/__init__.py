@@ -342,24 +342,29 @@ def qkv_rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
 
 
 def attention(q: torch.Tensor, kv_cache: torch.Tensor, layer: int, meta,
-              scale: float, sliding_window: Optional[int] = None) -> torch.Tensor:
+              scale: float, sliding_window: Optional[int] = None,
+              alibi_slopes: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Paged attention for a mixed batch: rows [0, num_decode) are single-token
     decode queries, the rest are (chunked) prefills reading the cached prefix.
+    ``alibi_slopes`` (fp32 [num_heads]) adds slope * (key pos - query pos) to
+    every score (ALiBi); those calls run the CUDA-core decode and mma.sync
+    prefill kernels.
     """
     if not q.is_cuda:
         return ref.paged_attention(q, kv_cache[:, layer, 0], kv_cache[:, layer, 1],
                                    meta.block_tables, meta.q_start, meta.seq_lens, scale,
-                                   sliding_window)
+                                   sliding_window, alibi_slopes)
     C = cuda_ext()
     out = torch.empty_like(q)
     win = int(sliding_window or 0)
     nd = meta.num_decode_seqs
     if nd > 0:
         _count(C.paged_decode(out, q, kv_cache, layer, meta.block_tables, meta.seq_lens, nd,
-                              meta.decode_splits, scale, win, meta.decode_workspace))
+                              meta.decode_splits, scale, win, meta.decode_workspace, alibi_slopes))
     if meta.num_seqs > nd:
         C.paged_prefill(out, q, kv_cache, layer, meta.block_tables, meta.q_start,
-                        meta.seq_lens, nd, meta.num_seqs, meta.max_q_len, scale, win)
+                        meta.seq_lens, nd, meta.num_seqs, meta.max_q_len, scale, win, -1,
+                        alibi_slopes)
         _count()
     return out
 

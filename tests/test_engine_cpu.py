@@ -161,3 +161,16 @@ def test_rejects_bad_prompts():
         llm.generate(prompt_token_ids=[[40000]], sampling_params=GREEDY, use_tqdm=False)
     with pytest.raises(ValueError):
         llm.generate(prompt_token_ids=[list(range(300))], sampling_params=GREEDY, use_tqdm=False)
+
+
+def test_alibi_model_generates_cpu():
+    """A model with ALiBi position bias (no RoPE) runs through the engine, and
+    the head slopes follow the ALiBi formula (2^-1 .. 2^-8 for 8 heads)."""
+    import torch
+    from swiftllm_b200.ops import reference as ref
+    a = LLM("tiny-llama-alibi", load_format="dummy", device="cpu", dtype="float32", max_num_seqs=4,
+            max_model_len=256)
+    out = a.generate(prompt_token_ids=PROMPTS[:2], sampling_params=GREEDY, use_tqdm=False)
+    assert all(len(o.outputs[0].token_ids) == 12 for o in out)
+    s = ref.alibi_slopes(8)
+    assert torch.allclose(s, torch.tensor([2.0 ** (-i) for i in range(1, 9)]))

@@ -453,3 +453,28 @@ def test_int8_model_gpu():
     out = llm.generate(prompt_token_ids=[list(range(100, 164))], sampling_params=sp, use_tqdm=False)
     assert len(out[0].outputs[0].token_ids) == 16
     llm.shutdown()
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(8, 8, 128), (8, 2, 128), (12, 4, 64)])
+def test_alibi_decode_and_prefill(C, Hq, Hkv, D):
+    # ALiBi: slope(head) * (key position - query position) added to every
+    # score, in the decode kernel (split and unsplit) and the prefill kernel
+    slopes = ref.alibi_slopes(Hq).float().cuda()
+    lens = [37, 300, 1, 129]
+    kv, bt, q_start, q, sl = _paged_setup(lens, [1] * len(lens), Hq, Hkv, D)
+    scale = 1 / math.sqrt(D)
+    r = ref.paged_attention(q.float().cpu(), kv[:, 1, 0].float().cpu(), kv[:, 1, 1].float().cpu(),
+                            bt.cpu(), q_start.cpu(), sl.cpu(), scale, alibi_slopes=slopes.cpu())
+    for splits in (1, 3):
+        ws = torch.empty(len(lens) * Hq * splits * (D + 2), dtype=torch.float32, device="cuda")
+        out = torch.empty_like(q)
+        C.paged_decode(out, q, kv, 1, bt, sl, len(lens), splits, scale, 0, ws, slopes)
+        torch.testing.assert_close(out.float().cpu(), r, rtol=2e-2, atol=2e-2)
+    pairs = [(64, 64), (300, 45), (17, 17), (200, 129)]
+    kv, bt, q_start, q, sl = _paged_setup([p[0] for p in pairs], [p[1] for p in pairs], Hq, Hkv, D)
+    out = torch.zeros_like(q)
+    C.paged_prefill(out, q, kv, 1, bt, q_start, sl, 0, len(pairs), 129, scale, 0, -1, slopes)
+    r = ref.paged_attention(q.float().cpu(), kv[:, 1, 0].float().cpu(), kv[:, 1, 1].float().cpu(),
+                            bt.cpu(), q_start.cpu(), sl.cpu(), scale, alibi_slopes=slopes.cpu())
+    torch.testing.assert_close(out.float().cpu(), r, rtol=2e-2, atol=2e-2)
+    _status_ok(C)

@@ -24,7 +24,7 @@ def _meta(T, dev):
                     logits_idx=torch.arange(T, dtype=torch.int32, device=dev))
 
 
-@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen2", "tiny-phi", "tiny-mixtral"])
+@pytest.mark.parametrize("name", ["tiny-llama", "tiny-qwen2", "tiny-phi", "tiny-mixtral", "tiny-llama-alibi"])
 def test_prefill_logits_gpu_vs_cpu(name):
     cfg = load_config(name)
     cpu = DecoderModel(cfg, torch.float32, "cpu")
