@@ -70,6 +70,8 @@ class LLMEngine:
     def __init__(self, config: EngineConfig):
         self.config = config
         self._initialized = False
+        from ..utils.profiler import StepProfiler
+        self._profiler = StepProfiler()
         self._reqs: Dict[str, _Req] = {}
         self._by_gid: Dict[int, _Req] = {}
         self._counter = 0
@@ -216,7 +218,9 @@ class LLMEngine:
             raise self._fatal
         from ..parallel.failures import CommTimeoutError, WorkerDiedError
         try:
-            return self._step()
+            outs = self._step()
+            self._profiler.step()
+            return outs
         except (WorkerDiedError, CommTimeoutError) as e:
             log.error("engine stopped: %s; aborting %d in-flight requests", e,
                       self.get_num_unfinished_requests())
@@ -560,6 +564,7 @@ class LLMEngine:
         }
 
     def shutdown(self) -> None:
+        self._profiler.close()
         if self.executor is not None:
             self.executor.shutdown()
             self.executor = None

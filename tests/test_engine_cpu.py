@@ -174,3 +174,16 @@ def test_alibi_model_generates_cpu():
     assert all(len(o.outputs[0].token_ids) == 12 for o in out)
     s = ref.alibi_slopes(8)
     assert torch.allclose(s, torch.tensor([2.0 ** (-i) for i in range(1, 9)]))
+
+
+def test_step_profiler_writes_trace(tmp_path, monkeypatch):
+    # SWIFTLLM_PROFILE records a window of engine steps with torch.profiler
+    monkeypatch.setenv("SWIFTLLM_PROFILE", str(tmp_path))
+    monkeypatch.setenv("SWIFTLLM_PROFILE_SKIP", "2")
+    monkeypatch.setenv("SWIFTLLM_PROFILE_STEPS", "3")
+    from swiftllm_b200 import LLM, SamplingParams
+    llm = LLM("tiny-llama", load_format="dummy", device="cpu", dtype="float32", max_model_len=128)
+    llm.generate(prompt_token_ids=[[1, 2, 3, 4]], use_tqdm=False,
+                 sampling_params=SamplingParams(temperature=0, max_tokens=8, ignore_eos=True))
+    assert (tmp_path / "trace.json").stat().st_size > 0
+    assert "Name" in (tmp_path / "summary.txt").read_text()
