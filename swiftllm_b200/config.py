@@ -41,6 +41,7 @@ class QuantizationMethod(Enum):
     GGUF = "gguf"
     FP8 = "fp8"
     INT8 = "int8"
+    INT4 = "int4"
 
 
 class SchedulerPolicy(Enum):

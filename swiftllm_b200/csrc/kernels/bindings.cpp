@@ -64,6 +64,9 @@ void moe_route(torch::Tensor logits, int64_t k, bool renorm, torch::Tensor w_out
 void moe_permute(torch::Tensor ids, int64_t e0, int64_t E_local, torch::Tensor offsets,
                  torch::Tensor perm_token, torch::Tensor inv_slot);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor weights, torch::Tensor inv_slot);
+void moe_gather(torch::Tensor xg, torch::Tensor x, torch::Tensor perm_token);
+int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
+                   int64_t M, int64_t group, c10::optional<torch::Tensor> bias);
 }  // namespace swift
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -110,4 +113,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route", &swift::moe_route);
   m.def("moe_permute", &swift::moe_permute);
   m.def("moe_combine", &swift::moe_combine);
+  m.def("gemm_w4a16", &swift::gemm_w4a16);
+  m.def("moe_gather", &swift::moe_gather);
 }

@@ -1,0 +1,510 @@
+// Weight-only int4 GEMM (W4A16: GPTQ / AWQ style group quantisation) on the
+// 5th-generation tensor cores.
+//
+//   Y[T, M] = X[T, K] . W[M, K]^T (+ bias),  W[m, k] = (q[m, k] - z[g, m]) * s[g, m]
+//   with q in [0, 15], g = k / group, bf16 activations and outputs.
+//
+// The reference declares gemm_int4 (crates/swiftllm-cuda/src/bindings.rs:245-288)
+// and the GPTQ / AWQ methods (crates/swiftllm-core/src/config.rs:184-215)
+// without a kernel. Decode is bound by weight bytes, so a 4-bit weight moves a
+// quarter of the bf16 bytes; the dequantisation happens in shared memory,
+// next to the tensor cores, and the MMA itself is the plain bf16
+// tcgen05.mma.kind::f16 with fp32 accumulators in TMEM.
+//
+// Weight layout (built once at load by ops.int4): qp [ceil(M/128), ceil(K/64),
+// 128, 32] bytes, so the 128 x 64 int4 tile of one (feature tile, k step) is
+// one contiguous 4 KB block fetched by a single cp.async.bulk. Inside a row,
+// the 4 bytes of 16-byte output chunk c (K elements 8c .. 8c+7) form one
+// little-endian word whose nibble at bit 4j holds element 2j and the nibble at
+// bit 16 + 4j holds element 2j + 1 (j = 0..3); then
+//   ((word >> 4j) & 0x000F000F) | 0x43004300
+// is the bf16 pair (128 + q[2j], 128 + q[2j+1]) with one LOP3 and a shift.
+// Per-(group, feature) parameters sz [G, Mpad] are bf16 pairs (128 + z, s):
+// (pair - (128 + z)) is exact in bf16 and the multiply by s rounds once, so
+// each dequantised weight equals bf16((q - z) * s) exactly.
+//
+// CTA (10 warps, one per SM, persistent over output tiles):
+//   warp 0      producer: cp.async.bulk of the 4 KB int4 tile + 2-D TMA of
+//               the BN x 64 activation tile (128-byte swizzle, no multicast)
+//               into a STAGES-deep ring;
+//   warp 1      TMEM allocation; one elected lane issues the MMAs;
+//               tcgen05.commit frees ring stages / publishes finished tiles;
+//   warps 2-5   epilogue: tcgen05.ld, bias, bf16 stores or fp32 split-K
+//               partials; two TMEM accumulators overlap tile i's epilogue
+//               with tile i+1's MMAs;
+//   warps 6-9   dequantisation: one thread per weight row expands 64 nibbles
+//               into the K-major 128-byte-swizzled bf16 A tile the MMA reads
+//               (chunk c of row r stored at chunk c ^ (r & 7)), then
+//               fence.proxy.async so the tensor core sees the writes.
+// Every mbarrier wait is bounded (status word + CTA abort flag; in-flight
+// copies and MMAs are drained and TMEM freed before the CTA returns).
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "tma_util.cuh"
+
+namespace swift {
+namespace w4 {
+
+constexpr int BM = 128, BK = 64;
+constexpr int kThreads = 320;
+constexpr int kRawBytes = BM * BK / 2;  // 4 KB of int4 per stage
+constexpr uint32_t kWaitLimit = 1u << 25;
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + kRawBytes;
+  static constexpr int TMEM_COLS = (2 * BN) <= 32    ? 32
+                                   : (2 * BN) <= 64  ? 64
+                                   : (2 * BN) <= 128 ? 128
+                                   : (2 * BN) <= 256 ? 256
+                                                     : 512;
+  static constexpr size_t BYTES = 1024 + size_t(STAGES) * STAGE_BYTES + 512;
+};
+
+__device__ __forceinline__ bool wait_one(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                         int* status, int where) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && *abort_flag) return false;
+  }
+  set_status(status, kErrWaitTimeout, where);
+  *abort_flag = 1;
+  return false;
+}
+// all lanes poll; the warp proceeds together
+__device__ __forceinline__ bool wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int where) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    if ((i & 255) == 255 && __any_sync(0xffffffffu, *abort_flag != 0)) return false;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    set_status(status, kErrWaitTimeout, where);
+    *abort_flag = 1;
+  }
+  return false;
+}
+__device__ __forceinline__ bool elect() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(pred));
+  return pred != 0;
+}
+// K-major, 128-byte swizzle descriptor (8-row atoms 1024 B apart, version 1)
+__device__ __forceinline__ uint64_t desc_sw128(const void* p) {
+  uint64_t d = static_cast<uint64_t>((smem_u32(p) & 0x3FFFF) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+// bf16 x bf16 -> f32, both K-major, N = BN, M = 128
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>(BM >> 4) << 24);
+}
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc));
+}
+__device__ __forceinline__ void commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ uint32_t bf2_as_u32(__nv_bfloat162 v) {
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ __nv_bfloat162 u32_as_bf2(uint32_t v) {
+  return *reinterpret_cast<__nv_bfloat162*>(&v);
+}
+// 8 int4 (one packed word, order above) -> 4 bf16 pairs (q - z) * s
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 zb, __nv_bfloat162 s) {
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t p = ((w >> (4 * j)) & 0x000F000Fu) | 0x43004300u;
+    o[j] = bf2_as_u32(__hmul2(__hsub2(u32_as_bf2(p), zb), s));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// qp: packed int4 tiles; sz: [G, Mpad] (128 + z, s) bf16 pairs; group is a
+// multiple of 64. ws: fp32 split-K partials [splits, N, M] when splits > 1.
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_x, const uint8_t* __restrict__ qp,
+                      const uint32_t* __restrict__ sz, __nv_bfloat16* __restrict__ y, int64_t ldy,
+                      const __nv_bfloat16* __restrict__ bias, float* __restrict__ ws, int M, int N,
+                      int K, int Mpad, int group, int splits, int* status) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* tiles =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + size_t(STAGES) * S::STAGE_BYTES);
+  uint64_t* afull = full + STAGES;   // dequantised A tile ready (4 warp arrivals)
+  uint64_t* empty = afull + STAGES;  // MMAs of the stage done
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int k_iters = (K + BK - 1) / BK;
+  const int k_per = (k_iters + splits - 1) / splits;
+  const int total = m_tiles * n_tiles * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&afull[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(S::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // tile t -> split s (outermost), feature tile m, token tile (n fastest, so
+  // CTAs running together share the weight tile through L2)
+  auto decode = [&](int t, int& m, int& x0, int& s) {
+    s = t / (m_tiles * n_tiles);
+    const int r = t % (m_tiles * n_tiles);
+    m = r / n_tiles;
+    x0 = (r % n_tiles) * BN;
+  };
+  auto stage = [&](int st) { return tiles + size_t(st) * S::STAGE_BYTES; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int m, x0, s;
+        decode(t, m, x0, s);
+        const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
+        for (int kk = k0; kk < k1; ++kk, ++it) {
+          const int st = it % STAGES;
+          if (!wait_one(&empty[st], ((it / STAGES) & 1) ^ 1, abort_flag, status, 40)) {
+            ok = false;
+            break;
+          }
+          uint8_t* a = stage(st);
+          mbar_arrive_expect_tx(&full[st], S::B_BYTES + kRawBytes);
+          tma_load_2d_nomc(a + S::A_BYTES, &tm_x, kk * BK, x0, &full[st]);
+          bulk_g2s(a + S::A_BYTES + S::B_BYTES,
+                   qp + (size_t(m) * k_iters + kk) * kRawBytes, kRawBytes, &full[st]);
+        }
+      }
+      if (!ok) {  // let issued copies land before the CTA exits
+        for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+          for (uint32_t p = 0; p < (1u << 20); ++p)
+            if (mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1)) break;
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t id = idesc<BN>();
+    uint32_t it = 0, tc = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tc) {
+      int m, x0, s;
+      decode(t, m, x0, s);
+      const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
+      const uint32_t buf = tc & 1;
+      if (!wait_warp(&tempty[buf], ((tc >> 1) & 1) ^ 1, abort_flag, status, 41)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const uint32_t d_tmem = tmem_base + buf * BN;
+      for (int kk = k0; kk < k1; ++kk, ++it) {
+        const int st = it % STAGES;
+        const uint32_t ph = (it / STAGES) & 1;
+        if (!wait_warp(&full[st], ph, abort_flag, status, 42) ||
+            !wait_warp(&afull[st], ph, abort_flag, status, 43)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        if (elect()) {
+          const uint8_t* a = stage(st);
+          const uint64_t ad = desc_sw128(a), bd = desc_sw128(a + S::A_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)  // +32 B along K inside the swizzle atom
+            mma(d_tmem, ad + 2 * j, bd + 2 * j, id, (kk > k0 || j > 0) ? 1u : 0u);
+          commit(&empty[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (elect()) commit(&tfull[buf]);
+      __syncwarp();
+    }
+    if (!ok && lane == 0) {  // issued MMAs finish (their commits arrive on empty[])
+      for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+        for (uint32_t p = 0; p < (1u << 20); ++p)
+          if (mbar_try_wait(&empty[j % STAGES], (j / STAGES) & 1)) break;
+    }
+  } else if (warp < 6) {
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
+      int m, x0, s;
+      decode(t, m, x0, s);
+      const uint32_t buf = tc & 1;
+      if (!wait_warp(&tfull[buf], (tc >> 1) & 1, abort_flag, status, 44)) break;
+      fence_after();
+      const int f = m * BM + q * 32 + lane;
+      const float b = (bias != nullptr && f < M && splits == 1) ? __bfloat162float(bias[f]) : 0.f;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      if constexpr (BN >= 32) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          ld32(tbase + c * 32, v);
+          const int t0 = x0 + c * 32;
+          if (f < M) {
+            if (splits == 1) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (t0 + j < N) y[int64_t(t0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (t0 + j < N) ws[(int64_t(s) * N + t0 + j) * M + f] = v[j];
+            }
+          }
+        }
+      } else {
+        float v[16];
+        ld16(tbase, v);
+        if (f < M) {
+          if (splits == 1) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (x0 + j < N) y[int64_t(x0 + j) * ldy + f] = __float2bfloat16(v[j] + b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (x0 + j < N) ws[(int64_t(s) * N + x0 + j) * M + f] = v[j];
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[buf]);
+    }
+  } else {
+    // dequantisation: thread r expands weight row r of the stage's tile
+    const int r = (warp - 6) * 32 + lane;
+    uint32_t it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x) {
+      int m, x0, s;
+      decode(t, m, x0, s);
+      const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
+      bool ok = true;
+      for (int kk = k0; kk < k1; ++kk, ++it) {
+        const int st = it % STAGES;
+        // (z, s) of this row's group: read before the wait (independent of it)
+        const uint32_t p = sz[size_t((kk * BK) / group) * Mpad + m * BM + r];
+        const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
+        const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
+        if (!wait_warp(&full[st], (it / STAGES) & 1, abort_flag, status, 45)) {
+          ok = false;
+          break;
+        }
+        uint8_t* a = stage(st);
+        const uint4* raw = reinterpret_cast<const uint4*>(a + S::A_BYTES + S::B_BYTES + r * 32);
+        const uint4 w0 = raw[0], w1 = raw[1];
+        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint8_t* row = a + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8(wv[c], zb, sc);
+        // generic-proxy smem writes -> visible to the tensor core (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[st]);
+      }
+      if (!ok) break;
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(S::TMEM_COLS));
+  }
+}
+
+__global__ void w4_splitk_reduce(__nv_bfloat16* __restrict__ y, int64_t ldy,
+                                 const float* __restrict__ ws, const __nv_bfloat16* __restrict__ bias,
+                                 int M, int N, int splits) {
+  const int64_t n = int64_t(M) * N;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / M), f = static_cast<int>(i % M);
+    float acc = bias ? __bfloat162float(bias[f]) : 0.f;
+    for (int s = 0; s < splits; ++s) acc += ws[int64_t(s) * n + i];
+    y[int64_t(t) * ldy + f] = __float2bfloat16(acc);
+  }
+}
+
+template <int BN, int STAGES>
+void launch(const CUtensorMap& tx, const uint8_t* qp, const uint32_t* sz, __nv_bfloat16* y,
+            int64_t ldy, const __nv_bfloat16* bias, float* ws, int M, int N, int K, int Mpad,
+            int group, int splits, int sms) {
+  using S = Smem<BN, STAGES>;
+  auto kern = gemm_w4a16_kernel<BN, STAGES>;
+  static bool attr[64] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr[dev]) {
+    SWIFT_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(S::BYTES)));
+    attr[dev] = true;
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
+  kern<<<std::min(tiles, sms), kThreads, S::BYTES, cur_stream()>>>(
+      tx, qp, sz, y, ldy, bias, ws, M, N, K, Mpad, group, splits, status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+}
+
+}  // namespace w4
+
+// out [T, M] bf16 = x [T, K] . dequant(qp, sz)^T (+ bias). qp uint8
+// [ceil(M/128), ceil(K/64), 128, 32] (tile-packed int4), sz int32 [G, Mpad]
+// ((128 + z, s) bf16 pairs), group a multiple of 64. Returns launches.
+int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
+                   int64_t M, int64_t group, c10::optional<torch::Tensor> bias) {
+  CHECK_BF16(x);
+  CHECK_BF16(out);
+  TORCH_CHECK(qp.scalar_type() == at::kByte && qp.is_contiguous() && qp.dim() == 4 &&
+                  qp.size(2) == w4::BM && qp.size(3) == w4::BK / 2,
+              "gemm_w4a16: qp must be uint8 [Mt, Kt, 128, 32]");
+  TORCH_CHECK(sz.scalar_type() == at::kInt && sz.is_contiguous() && sz.dim() == 2,
+              "gemm_w4a16: sz must be int32 [G, Mpad]");
+  TORCH_CHECK(group > 0 && group % w4::BK == 0, "gemm_w4a16: group must be a multiple of 64");
+  const int64_t K = x.size(-1), T = x.numel() / K;
+  const int64_t Mt = (M + w4::BM - 1) / w4::BM, Kt = (K + w4::BK - 1) / w4::BK;
+  TORCH_CHECK(qp.size(0) == Mt && qp.size(1) == Kt, "gemm_w4a16: qp tiles do not match M, K");
+  TORCH_CHECK(sz.size(1) == Mt * w4::BM && sz.size(0) >= (Kt * w4::BK + group - 1) / group,
+              "gemm_w4a16: sz shape");
+  TORCH_CHECK(x.stride(-1) == 1 && out.stride(-1) == 1, "gemm_w4a16: inner dims contiguous");
+  TORCH_CHECK(K % 8 == 0, "gemm_w4a16: K must be a multiple of 8 (16-byte TMA rows)");
+  const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
+  TORCH_CHECK(ldx % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(qp.data_ptr()) % 16 == 0,
+              "gemm_w4a16: 16-byte alignment");
+  TORCH_CHECK(out.numel() / out.size(-1) == T && out.size(-1) >= M);
+  if (T == 0) return 0;
+  const int64_t ldy = out.dim() >= 2 ? out.stride(-2) : M;
+  int dev;
+  cudaGetDevice(&dev);
+  static int sms_cache[64] = {0};
+  if (!sms_cache[dev]) cudaDeviceGetAttribute(&sms_cache[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sms_cache[dev];
+  // Token tile: one tile covers up to 256 tokens (each weight tile read once
+  // from HBM); narrower tiles while the grid leaves SMs idle (weight re-reads
+  // come from L2); split K only when that still leaves a quarter idle.
+  int bn;
+  if (T > 128) {
+    bn = 256;
+  } else {
+    bn = 16;
+    while (bn < T) bn *= 2;
+  }
+  while (bn > 32 && Mt * ((T + bn - 1) / bn) < sms * 3 / 4) bn /= 2;
+  const int64_t tiles = Mt * ((T + bn - 1) / bn);
+  int splits = 1;
+  if (tiles < sms * 3 / 4)
+    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, Kt / 4, 8})));
+  CUtensorMap tx = make_tmap_2d(x.data_ptr(), T, K, ldx, w4::BK, bn);
+  auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
+  const __nv_bfloat16* bp =
+      bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr<at::BFloat16>())
+                       : nullptr;
+  torch::Tensor ws;
+  float* wsp = nullptr;
+  if (splits > 1) {
+    ws = torch::empty({splits, T, M}, x.options().dtype(torch::kFloat));
+    wsp = ws.data_ptr<float>();
+  }
+  const uint8_t* q = qp.data_ptr<uint8_t>();
+  const uint32_t* s = reinterpret_cast<const uint32_t*>(sz.data_ptr<int32_t>());
+  const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K),
+            Mp = static_cast<int>(sz.size(1)), g = static_cast<int>(group);
+  switch (bn) {
+    case 16: w4::launch<16, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 32: w4::launch<32, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 64: w4::launch<64, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 128: w4::launch<128, 5>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    default: w4::launch<256, 4>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+  }
+  if (splits > 1) {
+    const int64_t n = M * T;
+    const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, sms * 8));
+    w4::w4_splitk_reduce<<<blocks, 256, 0, cur_stream()>>>(y, ldy, wsp, bp, Mi, Ni, splits);
+    SWIFT_CHECK_LAUNCH();
+    return 2;
+  }
+  return 1;
+}
+
+}  // namespace swift

@@ -5,11 +5,14 @@
 // mlp.rs:207-258) and create_model rejects Mixtral (architectures/mod.rs:68-76).
 //
 // moe_route_kernel: one warp per token, E <= 64 experts, k <= 8.
-// moe_permute: a single CTA counts rows per local expert, scans, and orders
-//   the (token, slot) pairs expert-contiguously so every expert's rows form
-//   one dense block for the grouped tcgen05 GEMM. Deterministic: rows keep
-//   token order inside an expert.
+// moe_permute: one CTA counts rows per local expert, scans, and orders the
+//   (token, slot) pairs expert-contiguously (warp match + per-warp scan) so
+//   every expert's rows form one dense block for the grouped tcgen05 GEMM.
+//   Deterministic: rows keep token order inside an expert.
+// moe_gather: the expert-ordered activation rows the grouped GEMM reads.
 // moe_combine: weighted sum of a token's expert outputs in slot order.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace swift {
@@ -63,43 +66,87 @@ __global__ void moe_route_kernel(const float* __restrict__ logits, int T, int E,
 // perm_token [T*k] (token of each expert-ordered row, rows past the total
 // stay 0) and inv_slot [T*k] (row of each (token, slot), -1 if the expert is
 // not local).
-__global__ void moe_permute_kernel(const int32_t* __restrict__ ids, int T, int k, int e0,
-                                   int E_local, int32_t* __restrict__ offsets,
-                                   int32_t* __restrict__ perm_token, int32_t* __restrict__ inv_slot) {
-  extern __shared__ int sh[];  // [E_local] counts then [E_local] cursors
-  int* cnt = sh;
-  int* cur = sh + E_local;
-  for (int e = threadIdx.x; e < E_local; e += blockDim.x) cnt[e] = 0;
-  for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
-    perm_token[i] = 0;
-    inv_slot[i] = -1;
-  }
+// One CTA of 1024 threads. Pass 1 counts rows per expert (shared atomics).
+// Pass 2 walks the (token, slot) list in chunks of 1024: inside a warp,
+// __match_any_sync groups lanes of the same expert and ranks them; a scan
+// over the 32 warps' per-expert counts (one thread per expert) turns them
+// into positions. Rows keep (token, slot) order inside an expert, so the
+// result is deterministic.
+constexpr int kPermThreads = 1024;
+__global__ void __launch_bounds__(kPermThreads)
+    moe_permute_kernel(const int32_t* __restrict__ ids, int T, int k, int e0, int E_local,
+                       int32_t* __restrict__ offsets, int32_t* __restrict__ perm_token,
+                       int32_t* __restrict__ inv_slot) {
+  __shared__ int cnt[64];
+  __shared__ int base[64];
+  __shared__ int wcnt[32][64];  // per warp, per expert: count, then first position
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = T * k;
+  for (int e = tid; e < 64; e += blockDim.x) cnt[e] = 0;
+  for (int j = tid; j < 32 * 64; j += blockDim.x) (&wcnt[0][0])[j] = 0;
+  for (int i = tid; i < n; i += blockDim.x) perm_token[i] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < T * k; i += blockDim.x) {
-    int e = ids[i] - e0;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const int e = ids[i] - e0;
     if (e >= 0 && e < E_local) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     int acc = 0;
     for (int e = 0; e < E_local; ++e) {
       offsets[e] = acc;
-      cur[e] = acc;
+      base[e] = acc;
       acc += cnt[e];
     }
     offsets[E_local] = acc;
   }
   __syncthreads();
-  // deterministic order: one thread per expert walks the (token, slot) list
-  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
-    int c = cur[e];
-    for (int i = 0; i < T * k; ++i) {
-      if (ids[i] - e0 == e) {
-        perm_token[c] = i / k;
-        inv_slot[i] = c;
-        ++c;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < n; c0 += blockDim.x) {
+    const int i = c0 + tid;
+    int e = i < n ? ids[i] - e0 : -1;
+    const bool local = e >= 0 && e < E_local;
+    if (!local) e = -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rk = __popc(same & lt);
+    if (local && rk == 0) wcnt[warp][e] = __popc(same);
+    __syncthreads();
+    if (tid < E_local) {
+      int run = base[tid];
+      for (int w = 0; w < 32; ++w) {
+        const int c = wcnt[w][tid];
+        wcnt[w][tid] = run;
+        run += c;
+      }
+      base[tid] = run;
+    }
+    __syncthreads();
+    if (i < n) {
+      if (local) {
+        const int pos = wcnt[warp][e] + rk;
+        perm_token[pos] = i / k;
+        inv_slot[i] = pos;
+      } else {
+        inv_slot[i] = -1;
       }
     }
+    __syncthreads();
+    for (int j = tid; j < 32 * 64; j += blockDim.x) (&wcnt[0][0])[j] = 0;
+    __syncthreads();
+  }
+}
+
+// xg[r] = x[perm_token[r]] for every expert-ordered row r < rows (16-byte
+// vectors; replaces a framework index_select before the grouped GEMM).
+__global__ void moe_gather_kernel(__nv_bfloat16* __restrict__ xg, const __nv_bfloat16* __restrict__ x,
+                                  const int32_t* __restrict__ perm, int rows, int H, int64_t ldx) {
+  const int vec = H / 8;
+  const int64_t total = int64_t(rows) * vec;
+  for (int64_t j = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; j < total;
+       j += int64_t(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(j / vec), c = static_cast<int>(j % vec);
+    const uint4 v = reinterpret_cast<const uint4*>(x + int64_t(perm[r]) * ldx)[c];
+    reinterpret_cast<uint4*>(xg + int64_t(r) * H)[c] = v;
   }
 }
 
@@ -140,10 +187,30 @@ void moe_route(torch::Tensor logits, int64_t k, bool renorm, torch::Tensor w_out
 void moe_permute(torch::Tensor ids, int64_t e0, int64_t E_local, torch::Tensor offsets,
                  torch::Tensor perm_token, torch::Tensor inv_slot) {
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous());
+  TORCH_CHECK(E_local >= 1 && E_local <= 64, "moe_permute: 1 <= local experts <= 64");
   const int T = static_cast<int>(ids.size(0)), k = static_cast<int>(ids.size(1));
-  moe_permute_kernel<<<1, 256, 2 * E_local * sizeof(int), cur_stream()>>>(
+  if (T * k == 0) return;
+  moe_permute_kernel<<<1, kPermThreads, 0, cur_stream()>>>(
       ids.data_ptr<int32_t>(), T, k, static_cast<int>(e0), static_cast<int>(E_local),
       offsets.data_ptr<int32_t>(), perm_token.data_ptr<int32_t>(), inv_slot.data_ptr<int32_t>());
+  SWIFT_CHECK_LAUNCH();
+}
+
+void moe_gather(torch::Tensor xg, torch::Tensor x, torch::Tensor perm_token) {
+  CHECK_BF16(xg);
+  CHECK_BF16(x);
+  TORCH_CHECK(perm_token.scalar_type() == at::kInt && perm_token.is_contiguous());
+  const int rows = static_cast<int>(perm_token.numel()), H = static_cast<int>(x.size(1));
+  TORCH_CHECK(xg.is_contiguous() && xg.size(0) >= rows && xg.size(1) == H && H % 8 == 0);
+  TORCH_CHECK(x.stride(1) == 1 && x.stride(0) % 8 == 0 &&
+              reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "moe_gather: 16-byte rows");
+  if (!rows) return;
+  const int64_t vecs = int64_t(rows) * (H / 8);
+  const int blocks = static_cast<int>(std::min<int64_t>((vecs + 255) / 256, 148 * 16));
+  moe_gather_kernel<<<blocks, 256, 0, cur_stream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(xg.data_ptr<at::BFloat16>()),
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>()),
+      perm_token.data_ptr<int32_t>(), rows, H, x.stride(0));
   SWIFT_CHECK_LAUNCH();
 }
 

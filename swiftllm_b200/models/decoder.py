@@ -186,6 +186,9 @@ class DecoderModel:
                 if isinstance(v, (ops.Fp8Weight, ops.Int8Weight)):
                     yield f"layers.{i}.{k}.q", v.q
                     yield f"layers.{i}.{k}.scale", v.scale
+                elif isinstance(v, ops.Int4Weight):
+                    yield f"layers.{i}.{k}.qp", v.qp
+                    yield f"layers.{i}.{k}.sz", v.sz
                 elif isinstance(v, torch.Tensor):
                     yield f"layers.{i}.{k}", v
         yield "norm", self.norm_w
@@ -260,6 +263,24 @@ class DecoderModel:
                 w = getattr(L, name, None)
                 if isinstance(w, torch.Tensor) and w.dim() == 2:
                     setattr(L, name, ops.int8_weight(w))
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def quantize_int4(self, group: int = 128) -> None:
+        """W4A16: the dense projection weights (QKV, o_proj, gate_up / fc1,
+        down / fc2) become int4 codes with a bf16 scale and zero point per
+        ``group`` input features (round to nearest; GPTQ / AWQ checkpoints
+        arrive here dequantised and are re-packed with their own group size).
+        Activations stay bf16. Embedding, norms, LM head and MoE experts stay
+        in the model dtype. The kernel's groups are multiples of 64 input
+        features: a per-channel checkpoint (group <= 0) uses one group per
+        row, and a smaller group is widened to 64."""
+        for L in self.layers:
+            for name in ("wqkv", "wo", "w13", "w1", "w2"):
+                w = getattr(L, name, None)
+                if isinstance(w, torch.Tensor) and w.dim() == 2:
+                    g = -(-w.shape[1] // 64) * 64 if group <= 0 else -(-group // 64) * 64
+                    setattr(L, name, ops.int4.quantize(w, g))
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
 

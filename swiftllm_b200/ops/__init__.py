@@ -143,6 +143,10 @@ class Int8Weight:
         return self.q.float() * self.scale[:, None]
 
 
+from . import int4  # noqa: E402
+from .int4 import Int4Weight  # noqa: E402
+
+
 def quantize_s8(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row symmetric int8: (int8 [R, K], fp32 scale [R]), scale =
     max|row| / 127, round to nearest even."""
@@ -231,6 +235,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
         return _linear_fp8(x, w, b, out)
     if isinstance(w, Int8Weight):
         return _linear_int8(x, w, b, out)
+    if isinstance(w, Int4Weight):
+        return int4.linear(x, w, b, out)
     if not x.is_cuda:
         return ref.linear(x, w, b)
     if _GEMM_BACKEND == "cublas" or (_GEMM_BACKEND == "auto" and _library_faster(x, w)):

@@ -48,8 +48,9 @@ def moe_forward(model, L, x: torch.Tensor) -> torch.Tensor:
     perm = torch.empty(T * k, dtype=torch.int32, device=x.device)
     inv = torch.empty(T * k, dtype=torch.int32, device=x.device)
     C.moe_permute(ids, model.e0, El, offsets, perm, inv)
-    ops._count(2)
-    xg = x.index_select(0, perm)
+    xg = torch.empty(T * k, H, dtype=x.dtype, device=x.device)
+    C.moe_gather(xg, x, perm)
+    ops._count(3)
     avg = max(1, (T * k) // max(c.num_experts, 1))
     I2 = L.w13.shape[1]
     h = torch.empty(T * k, I2, dtype=x.dtype, device=x.device)

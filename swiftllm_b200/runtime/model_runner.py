@@ -134,19 +134,29 @@ class ModelRunner:
         self.model.allocate()
         fmt = self.ecfg.load_format
         model = self.ecfg.model
+        q = getattr(self.ecfg.quantization, "value", self.ecfg.quantization)
+        group = 128
         if fmt == "dummy" or (fmt == "auto" and not os.path.exists(model)):
             self.model.init_dummy(seed=self.ecfg.seed)
         else:
             from ..loaders import open_checkpoint
+            from ..loaders.quantized import wrap_quantized
             ckpt = open_checkpoint(model, fmt)
-            self.model.load_state(ckpt.get)
-        q = getattr(self.ecfg.quantization, "value", self.ecfg.quantization)
+            get, found = wrap_quantized(ckpt.get, model)
+            if found is not None:  # GPTQ / AWQ tensors: dequantised here, re-packed below
+                group = found[1]
+                if q in (None, "none"):
+                    q = "int4"
+            self.model.load_state(get)
         if q == "fp8":
             self.model.quantize_fp8()
         elif q == "int8":
             self.model.quantize_int8()
+        elif q in ("int4", "gptq", "awq"):
+            self.model.quantize_int4(group)
         elif q not in (None, "none"):
-            raise NotImplementedError(f"quantization {q!r} is not supported (fp8 and int8 are)")
+            raise NotImplementedError(f"quantization {q!r} is not supported "
+                                      "(fp8, int8, int4 / gptq / awq are)")
         elif (self.is_cuda and ops.gemm_backend() == "tcgen05"
               and os.environ.get("SWIFTLLM_FUSE_SWIGLU", "1") != "0"):
             # our GEMMs everywhere: SwiGLU in the gate/up GEMM epilogue

@@ -322,7 +322,9 @@ def test_moe_route_permute_grouped_gemm_combine(C):
         x = bf(T, H)
         w13 = bf(El, 2 * I, H, scale=0.05)
         w2 = bf(El, H, I, scale=0.05)
-        xg = x.index_select(0, perm)
+        xg = torch.empty(T * k, H, dtype=torch.bfloat16, device="cuda")
+        C.moe_gather(xg, x, perm)
+        assert torch.equal(xg, x.index_select(0, perm))
         h = torch.empty(T * k, 2 * I, dtype=torch.bfloat16, device="cuda")
         C.gemm_grouped(h, xg, w13, off, T * k // E)
         a = torch.empty(T * k, I, dtype=torch.bfloat16, device="cuda")
@@ -339,6 +341,31 @@ def test_moe_route_permute_grouped_gemm_combine(C):
             hh = R.silu_and_mul(x.float().cpu()[rows] @ w13[le].float().cpu().t())
             ref.index_add_(0, rows, (hh @ w2[le].float().cpu().t()) * w.cpu()[rows, slot].unsqueeze(1))
         torch.testing.assert_close(out.float().cpu(), ref, rtol=3e-2, atol=3e-2)
+    _status_ok(C)
+
+
+@pytest.mark.parametrize("T,k,E,e0,El", [(1, 2, 8, 0, 8), (3000, 2, 8, 2, 3), (517, 8, 64, 5, 40)])
+def test_moe_permute_order(C, T, k, E, e0, El):
+    # expert-contiguous rows, (token, slot) order inside an expert, against
+    # a plain-Python stable ordering; chunks of 1024 pairs cross warps
+    g = torch.Generator().manual_seed(T)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).int()
+    off = torch.empty(El + 1, dtype=torch.int32, device="cuda")
+    perm = torch.empty(T * k, dtype=torch.int32, device="cuda")
+    inv = torch.empty(T * k, dtype=torch.int32, device="cuda")
+    C.moe_permute(ids.cuda(), e0, El, off, perm, inv)
+    flat = ids.view(-1).tolist()
+    want_perm, want_inv, want_off = [], [-1] * (T * k), [0]
+    for e in range(e0, e0 + El):
+        for i, v in enumerate(flat):
+            if v == e:
+                want_inv[i] = len(want_perm)
+                want_perm.append(i // k)
+        want_off.append(len(want_perm))
+    n = len(want_perm)
+    assert off.cpu().tolist() == want_off
+    assert perm.cpu()[:n].tolist() == want_perm and perm.cpu()[n:].eq(0).all()
+    assert inv.cpu().tolist() == want_inv
     _status_ok(C)
 
 
