@@ -247,3 +247,103 @@ void sample(torch::Tensor tokens, torch::Tensor lps, torch::Tensor logits, torch
 }
 
 }  // namespace swift
+
+namespace swift {
+
+// Greedy verification of speculative drafts, one CTA per verified position:
+// over the row's logits x / t it finds the arg-max (lowest index among ties,
+// like torch.argmax), the log-sum-exp, and writes
+//   out[0][i] = 1 if arg-max == draft[i] else 0     (accepted)
+//   out[1][i] = arg-max                              (replacement token)
+//   out[2][i] = log p(draft[i]),  out[3][i] = log p(arg-max)
+// as one fp32 [4, M] block, so the host reads the whole verdict with one copy.
+// Parity: crates/swiftllm-core/src/execution/speculative.rs:97-190 (verify).
+constexpr int kVerThreads = 512;
+__global__ void __launch_bounds__(kVerThreads)
+    spec_verify_greedy_kernel(const float* __restrict__ logits, int64_t ld, int V,
+                              const int64_t* __restrict__ pos, const int64_t* __restrict__ draft,
+                              const float* __restrict__ temp, int M, float* __restrict__ out) {
+  const int i = blockIdx.x;
+  const float* x = logits + pos[i] * ld;
+  const float inv_t = 1.f / temp[i];
+  __shared__ float s_v[32];
+  __shared__ int s_i[32];
+  __shared__ float s_sum[32];
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float y = x[v] * inv_t;
+    if (y > bv) {  // strided ascending walk: the first hit of a tie keeps the lowest index
+      bv = y;
+      bi = v;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    s_v[warp] = bv;
+    s_i[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    bv = lane < nw ? s_v[lane] : -INFINITY;
+    bi = lane < nw ? s_i[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      s_v[0] = bv;
+      s_i[0] = bi;
+    }
+  }
+  __syncthreads();
+  const float mx = s_v[0];
+  const int am = s_i[0];
+  float sum = 0.f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) sum += __expf(x[v] * inv_t - mx);
+  sum = warp_sum(sum);
+  if (lane == 0) s_sum[warp] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float z = 0.f;
+    for (int w = 0; w < nw; ++w) z += s_sum[w];
+    const float lz = mx + logf(z);
+    const int64_t d = draft[i];
+    const bool in_range = d >= 0 && d < V;
+    out[i] = (in_range && d == am) ? 1.f : 0.f;
+    out[M + i] = static_cast<float>(am);
+    out[2 * M + i] = in_range ? x[d] * inv_t - lz : -INFINITY;
+    out[3 * M + i] = mx - lz;
+  }
+}
+
+// logits fp32 [R, V] (row stride ld), pos / draft int64 [M], temp fp32 [M]
+// (1 for greedy rows), out fp32 [4, M].
+void spec_verify_greedy(torch::Tensor logits, torch::Tensor pos, torch::Tensor draft,
+                        torch::Tensor temp, torch::Tensor out) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(-1) == 1);
+  TORCH_CHECK(pos.scalar_type() == at::kLong && draft.scalar_type() == at::kLong &&
+              temp.scalar_type() == at::kFloat && out.scalar_type() == at::kFloat);
+  const int M = static_cast<int>(pos.numel());
+  TORCH_CHECK(draft.numel() == M && temp.numel() == M && out.numel() == 4 * M && out.is_contiguous());
+  if (!M) return;
+  spec_verify_greedy_kernel<<<M, kVerThreads, 0, cur_stream()>>>(
+      logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(-1)),
+      pos.data_ptr<int64_t>(), draft.data_ptr<int64_t>(), temp.data_ptr<float>(), M,
+      out.data_ptr<float>());
+  SWIFT_CHECK_LAUNCH();
+}
+
+}  // namespace swift

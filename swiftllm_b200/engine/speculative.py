@@ -332,9 +332,17 @@ class SpeculativeDecoder:
         dev = logits.device
         pos = torch.from_numpy(vpos).to(dev)
         d = torch.from_numpy(vdraft).to(dev)
-        x = logits.index_select(0, pos).float()
         greedy = (temp[vrow] == 0) | (topk[vrow] == 1)
         t = torch.from_numpy(np.where(temp[vrow] > 0, temp[vrow], 1.0).astype(np.float32)).to(dev)
+        if greedy.all() and logits.is_cuda and logits.dtype == torch.float32:
+            # one kernel: arg-max, log-sum-exp and both log-probabilities per position
+            from .. import ops
+            out = torch.empty(4, len(vpos), dtype=torch.float32, device=dev)
+            ops.cuda_ext().spec_verify_greedy(logits, pos, d, t, out)
+            ops._count()
+            both = out.cpu().numpy()
+            return both[0] > 0.5, both[1].astype(np.int64), both[2], both[3]
+        x = logits.index_select(0, pos).float()
         lsm = torch.log_softmax(x / t.unsqueeze(1), dim=-1)
         am = x.argmax(-1)
         acc = am == d

@@ -148,7 +148,10 @@ class DecoderModel:
         c = self.cfg
         H, D = c.hidden_size, c.head_dim
         qkv_rows = (self.local_heads + 2 * self.local_kv_heads) * D
-        self.embed = self._alloc(c.vocab_size, H)
+        # vocab-parallel embedding: each rank keeps the rows of its vocabulary
+        # slice (the LM head's slice); lookups outside it give zero rows and
+        # the cross-rank sum of the first reduction completes them
+        self.embed = self._alloc(self.vocab_end - self.vocab_start, H)
         self.layers = []
         for _ in range(c.num_layers):
             L = SimpleNamespace()
@@ -249,7 +252,7 @@ class DecoderModel:
             if c.num_experts:
                 return ("cols3", c.intermediate_size, r * self.local_inter)
             return ("cols", c.intermediate_size, r * self.local_inter)
-        if leaf in ("lm_head", "lm_head_b") and self.vocab_end - self.vocab_start != c.vocab_size:
+        if leaf in ("lm_head", "lm_head_b", "embed") and self.vocab_end - self.vocab_start != c.vocab_size:
             return ("rows", c.vocab_size, [(0, self.vocab_start, self.vocab_end - self.vocab_start)])
         return None
 
@@ -384,8 +387,15 @@ class DecoderModel:
         (``tp.reduce_norm``). Returns the final-normed rows of logits_idx."""
         c = self.cfg
         T, H = int(input_ids.shape[0]), c.hidden_size
-        h = ops.embedding(input_ids, self.embed)  # residual (own token rows kept current)
-        x, _ = self._norm(h, self.layers[0].ln1, None)
+        if self.vocab_parallel:
+            # partial lookups of every rank's vocabulary slice, summed by the
+            # first reduction, which also norms and all-gathers them
+            ops.embedding(input_ids, self.embed, self.vocab_start, out=self.tp.reduce_buffer(T, H))
+            h = torch.zeros(T, H, dtype=self.embed.dtype, device=self.embed.device)
+            x = self.tp.reduce_norm(T, h, self.layers[0].ln1, c.rms_norm_eps)
+        else:
+            h = ops.embedding(input_ids, self.embed)  # residual (own token rows kept current)
+            x, _ = self._norm(h, self.layers[0].ln1, None)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
             q = ops.qkv_rope_cache(ops.linear(x, L.wqkv), meta.positions, self.cos_sin, kv_cache, i,
@@ -412,7 +422,10 @@ class DecoderModel:
         c = self.cfg
         if self._seq_parallel():
             return self._forward_seq_parallel(input_ids, meta, kv_cache)
-        h = ops.embedding(input_ids, self.embed)
+        if self.vocab_parallel:  # VocabParallelEmbedding: zero rows off-slice, then the sum
+            h = self.tp.reduce(ops.embedding(input_ids, self.embed, self.vocab_start))
+        else:
+            h = ops.embedding(input_ids, self.embed)
         residual = None
         for i, L in enumerate(self.layers):
             if c.parallel_block:

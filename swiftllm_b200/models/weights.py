@@ -35,7 +35,7 @@ def load_hf_weights(model, get: Callable[[str], Optional[torch.Tensor]]) -> None
             raise KeyError(f"checkpoint is missing {name}")
         return t
 
-    _copy(model.embed, need("model.embed_tokens.weight"), "embed")
+    _copy(model.embed, need("model.embed_tokens.weight")[model.vocab_start:model.vocab_end], "embed")
     for i, L in enumerate(model.layers):
         p = f"model.layers.{i}."
         _copy(L.ln1, need(p + "input_layernorm.weight"), "ln1")

@@ -306,16 +306,21 @@ def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0) -> torch.Tensor:
+def embedding(ids: torch.Tensor, w: torch.Tensor, vocab_start: int = 0,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Rows of ``w`` for ``ids``; with ``vocab_start`` (vocab-parallel shard)
     ids outside [vocab_start, vocab_start + rows) give zero rows."""
     if not ids.is_cuda:
         local = ids.long() - vocab_start
         ok = (local >= 0) & (local < w.shape[0])
-        out = w[local.clamp(0, w.shape[0] - 1)].clone()
-        out[~ok] = 0
-        return out
-    out = torch.empty((ids.shape[0], w.shape[1]), dtype=w.dtype, device=w.device)
+        res = w[local.clamp(0, w.shape[0] - 1)].clone()
+        res[~ok] = 0
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
+    if out is None:
+        out = torch.empty((ids.shape[0], w.shape[1]), dtype=w.dtype, device=w.device)
     cuda_ext().embedding(out, ids, w, vocab_start)
     _count()
     return out

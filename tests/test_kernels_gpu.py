@@ -505,3 +505,26 @@ def test_alibi_decode_and_prefill(C, Hq, Hkv, D):
                             bt.cpu(), q_start.cpu(), sl.cpu(), scale, alibi_slopes=slopes.cpu())
     torch.testing.assert_close(out.float().cpu(), r, rtol=2e-2, atol=2e-2)
     _status_ok(C)
+
+
+def test_spec_verify_greedy(C):
+    # arg-max (lowest index on ties), accept flag and log-probabilities of
+    # the draft and arg-max tokens against torch on the same rows
+    V, R = 32003, 9
+    logits = torch.randn(R, V, device="cuda") * 3
+    logits[2, 100] = logits[2, 7] = 50.0  # tie: index 7 wins
+    pos = torch.tensor([0, 2, 2, 5, 8, 8], dtype=torch.int64, device="cuda")
+    am = logits.argmax(-1)
+    draft = torch.stack([am[0], torch.tensor(100, device="cuda"), am[2], am[5] + 1,
+                         am[8], torch.tensor(3, device="cuda")]).to(torch.int64)
+    temp = torch.tensor([1.0, 1.0, 0.7, 1.0, 2.0, 1.0], device="cuda")
+    out = torch.empty(4, 6, device="cuda")
+    C.spec_verify_greedy(logits, pos, draft, temp, out)
+    x = logits.index_select(0, pos) / temp[:, None]
+    lsm = torch.log_softmax(x, -1)
+    ref_am = x.argmax(-1)
+    assert out[1].long().tolist() == ref_am.tolist() and ref_am[1].item() == 7
+    assert (out[0] > 0.5).tolist() == (ref_am == draft).tolist()
+    torch.testing.assert_close(out[2], lsm.gather(1, draft[:, None]).view(-1), rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(out[3], lsm.gather(1, ref_am[:, None]).view(-1), rtol=1e-4, atol=1e-4)
+    _status_ok(C)
