@@ -65,6 +65,8 @@ void moe_permute(torch::Tensor ids, int64_t e0, int64_t E_local, torch::Tensor o
                  torch::Tensor perm_token, torch::Tensor inv_slot);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor weights, torch::Tensor inv_slot);
 void moe_gather(torch::Tensor xg, torch::Tensor x, torch::Tensor perm_token);
+void spec_verify_greedy(torch::Tensor logits, torch::Tensor pos, torch::Tensor draft,
+                        torch::Tensor temp, torch::Tensor out);
 int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
                    int64_t M, int64_t group, c10::optional<torch::Tensor> bias);
 }  // namespace swift
@@ -115,4 +117,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &swift::moe_combine);
   m.def("gemm_w4a16", &swift::gemm_w4a16);
   m.def("moe_gather", &swift::moe_gather);
+  m.def("spec_verify_greedy", &swift::spec_verify_greedy);
 }

@@ -23,19 +23,27 @@
 // (pair - (128 + z)) is exact in bf16 and the multiply by s rounds once, so
 // each dequantised weight equals bf16((q - z) * s) exactly.
 //
-// CTA (10 warps, one per SM, persistent over output tiles):
-//   warp 0      producer: cp.async.bulk of the 4 KB int4 tile + 2-D TMA of
-//               the BN x 64 activation tile (128-byte swizzle, no multicast)
-//               into a STAGES-deep ring;
+// CTA (22 warps, one per SM, persistent over output tiles), two rings:
+//   codes ring (RSTAGES slots of 4.5 KB: the 4 KB int4 tile of one k step
+//   and the 512-byte (z, s) row of its group) and operand ring (STAGES
+//   slots: the bf16 A tile the dequantisation writes and the BN x 64
+//   activation tile). A codes slot is 1/4 of an operand slot, so the codes
+//   ring runs 6-16 k steps ahead and keeps enough bytes in flight per SM
+//   to stream the weights at HBM rate.
+//   warp 0      codes producer: two cp.async.bulk per k step;
 //   warp 1      TMEM allocation; one elected lane issues the MMAs;
-//               tcgen05.commit frees ring stages / publishes finished tiles;
+//               tcgen05.commit frees operand stages / publishes finished tiles;
 //   warps 2-5   epilogue: tcgen05.ld, bias, bf16 stores or fp32 split-K
 //               partials; two TMEM accumulators overlap tile i's epilogue
 //               with tile i+1's MMAs;
-//   warps 6-9   dequantisation: one thread per weight row expands 64 nibbles
-//               into the K-major 128-byte-swizzled bf16 A tile the MMA reads
-//               (chunk c of row r stored at chunk c ^ (r & 7)), then
-//               fence.proxy.async so the tensor core sees the writes.
+//   warps 6-21  dequantisation, 4 groups of 4 warps taking k steps round
+//               robin: wait for the operand stage to be free (the group's
+//               first warp then requests its activation tile by 2-D TMA,
+//               128-byte swizzle, no multicast), read the codes (freeing the
+//               codes slot), one thread per weight row expands 64 nibbles
+//               into the K-major 128-byte-swizzled bf16 A tile (chunk c of
+//               row r stored at chunk c ^ (r & 7)), then fence.proxy.async
+//               so the tensor core sees the writes.
 // Every mbarrier wait is bounded (status word + CTA abort flag; in-flight
 // copies and MMAs are drained and TMEM freed before the CTA returns).
 #include <cudaTypedefs.h>
@@ -49,21 +57,25 @@ namespace swift {
 namespace w4 {
 
 constexpr int BM = 128, BK = 64;
-constexpr int kThreads = 320;
+constexpr int kDqGroups = 4;                     // dequantisation groups of 4 warps
+constexpr int kThreads = (6 + 4 * kDqGroups) * 32;  // 704
 constexpr int kRawBytes = BM * BK / 2;  // 4 KB of int4 per stage
+constexpr int kScBytes = BM * 4;        // (128 + z, s) of the stage's 128 rows
+constexpr int kRawRegion = kRawBytes + kScBytes;  // one codes-ring slot
 constexpr uint32_t kWaitLimit = 1u << 25;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int RSTAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES + kRawBytes;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // bf16 operands of one k step
   static constexpr int TMEM_COLS = (2 * BN) <= 32    ? 32
                                    : (2 * BN) <= 64  ? 64
                                    : (2 * BN) <= 128 ? 128
                                    : (2 * BN) <= 256 ? 256
                                                      : 512;
-  static constexpr size_t BYTES = 1024 + size_t(STAGES) * STAGE_BYTES + 512;
+  static constexpr size_t BYTES =
+      1024 + size_t(STAGES) * STAGE_BYTES + size_t(RSTAGES) * kRawRegion + 512;
 };
 
 __device__ __forceinline__ bool wait_one(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
@@ -171,20 +183,23 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 zb, __nv_bf
 
 // qp: packed int4 tiles; sz: [G, Mpad] (128 + z, s) bf16 pairs; group is a
 // multiple of 64. ws: fp32 split-K partials [splits, N, M] when splits > 1.
-template <int BN, int STAGES>
+template <int BN, int STAGES, int RSTAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_x, const uint8_t* __restrict__ qp,
                       const uint32_t* __restrict__ sz, __nv_bfloat16* __restrict__ y, int64_t ldy,
                       const __nv_bfloat16* __restrict__ bias, float* __restrict__ ws, int M, int N,
                       int K, int Mpad, int group, int splits, int* status) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, RSTAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(tiles + size_t(STAGES) * S::STAGE_BYTES);
-  uint64_t* afull = full + STAGES;   // dequantised A tile ready (4 warp arrivals)
-  uint64_t* empty = afull + STAGES;  // MMAs of the stage done
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* rring = tiles + size_t(STAGES) * S::STAGE_BYTES;  // int4 codes + (z, s) rows
+  uint64_t* bfull = reinterpret_cast<uint64_t*>(rring + size_t(RSTAGES) * kRawRegion);
+  uint64_t* afull = bfull + STAGES;    // dequantised A tile written (4 warp arrivals)
+  uint64_t* abempty = afull + STAGES;  // MMAs of the operand stage done
+  uint64_t* rfull = abempty + STAGES;  // codes + scales landed
+  uint64_t* rempty = rfull + RSTAGES;  // codes read by the dequantisation warps (4 arrivals)
+  uint64_t* tfull = rempty + RSTAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -198,9 +213,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&bfull[s], 1);
       mbar_init(&afull[s], 4);
-      mbar_init(&empty[s], 1);
+      mbar_init(&abempty[s], 1);
+    }
+    for (int s = 0; s < RSTAGES; ++s) {
+      mbar_init(&rfull[s], 1);
+      mbar_init(&rempty[s], 4);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
@@ -229,8 +248,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     x0 = (r % n_tiles) * BN;
   };
   auto stage = [&](int st) { return tiles + size_t(st) * S::STAGE_BYTES; };
+  auto rstage = [&](int r) { return rring + size_t(r) * kRawRegion; };
 
   if (warp == 0) {
+    // codes producer: runs up to RSTAGES k steps ahead of the dequantisation
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
@@ -239,22 +260,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode(t, m, x0, s);
         const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
         for (int kk = k0; kk < k1; ++kk, ++it) {
-          const int st = it % STAGES;
-          if (!wait_one(&empty[st], ((it / STAGES) & 1) ^ 1, abort_flag, status, 40)) {
+          const int r = it % RSTAGES;
+          if (!wait_one(&rempty[r], ((it / RSTAGES) & 1) ^ 1, abort_flag, status, 40)) {
             ok = false;
             break;
           }
-          uint8_t* a = stage(st);
-          mbar_arrive_expect_tx(&full[st], S::B_BYTES + kRawBytes);
-          tma_load_2d_nomc(a + S::A_BYTES, &tm_x, kk * BK, x0, &full[st]);
-          bulk_g2s(a + S::A_BYTES + S::B_BYTES,
-                   qp + (size_t(m) * k_iters + kk) * kRawBytes, kRawBytes, &full[st]);
+          uint8_t* dst = rstage(r);
+          mbar_arrive_expect_tx(&rfull[r], kRawBytes + kScBytes);
+          bulk_g2s(dst, qp + (size_t(m) * k_iters + kk) * kRawBytes, kRawBytes, &rfull[r]);
+          // the 128 rows' (z, s) words of this k step's group: 512 contiguous bytes
+          bulk_g2s(dst + kRawBytes, sz + size_t((kk * BK) / group) * Mpad + m * BM, kScBytes,
+                   &rfull[r]);
         }
       }
       if (!ok) {  // let issued copies land before the CTA exits
-        for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+        for (uint32_t j = it > RSTAGES ? it - RSTAGES : 0; j < it; ++j)
           for (uint32_t p = 0; p < (1u << 20); ++p)
-            if (mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1)) break;
+            if (mbar_try_wait(&rfull[j % RSTAGES], (j / RSTAGES) & 1)) break;
       }
     }
   } else if (warp == 1) {
@@ -275,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = k0; kk < k1; ++kk, ++it) {
         const int st = it % STAGES;
         const uint32_t ph = (it / STAGES) & 1;
-        if (!wait_warp(&full[st], ph, abort_flag, status, 42) ||
+        if (!wait_warp(&bfull[st], ph, abort_flag, status, 42) ||
             !wait_warp(&afull[st], ph, abort_flag, status, 43)) {
           ok = false;
           break;
@@ -287,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < BK / 16; ++j)  // +32 B along K inside the swizzle atom
             mma(d_tmem, ad + 2 * j, bd + 2 * j, id, (kk > k0 || j > 0) ? 1u : 0u);
-          commit(&empty[st]);
+          commit(&abempty[st]);
         }
         __syncwarp();
       }
@@ -295,10 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (elect()) commit(&tfull[buf]);
       __syncwarp();
     }
-    if (!ok && lane == 0) {  // issued MMAs finish (their commits arrive on empty[])
+    if (!ok && lane == 0) {  // issued MMAs finish (their commits arrive on abempty[])
       for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
         for (uint32_t p = 0; p < (1u << 20); ++p)
-          if (mbar_try_wait(&empty[j % STAGES], (j / STAGES) & 1)) break;
+          if (mbar_try_wait(&abempty[j % STAGES], (j / STAGES) & 1)) break;
     }
   } else if (warp < 6) {
     const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -350,8 +372,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
   } else {
-    // dequantisation: thread r expands weight row r of the stage's tile
-    const int r = (warp - 6) * 32 + lane;
+    // dequantisation (warps 6..): kDqGroups groups of 4 warps take k steps
+    // round robin, so that many stages are expanded at once (one group's
+    // wait / convert / fence chain is ~0.5 us per k step); thread r of a
+    // group expands weight row r. Before writing operand stage st the group
+    // waits for its previous MMAs; the group's first warp then requests that
+    // stage's activation tile.
+    const int dw = warp - 6, grp = dw >> 2;
+    const bool leader = (dw & 3) == 0;
+    const int r = (dw & 3) * 32 + lane;
     uint32_t it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int m, x0, s;
@@ -359,18 +388,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int k0 = s * k_per, k1 = min(k_iters, k0 + k_per);
       bool ok = true;
       for (int kk = k0; kk < k1; ++kk, ++it) {
-        const int st = it % STAGES;
-        // (z, s) of this row's group: read before the wait (independent of it)
-        const uint32_t p = sz[size_t((kk * BK) / group) * Mpad + m * BM + r];
-        const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
-        const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
-        if (!wait_warp(&full[st], (it / STAGES) & 1, abort_flag, status, 45)) {
+        if (static_cast<int>(it % kDqGroups) != grp) continue;
+        const int st = it % STAGES, rs = it % RSTAGES;
+        if (!wait_warp(&abempty[st], ((it / STAGES) & 1) ^ 1, abort_flag, status, 45)) {
           ok = false;
           break;
         }
         uint8_t* a = stage(st);
-        const uint4* raw = reinterpret_cast<const uint4*>(a + S::A_BYTES + S::B_BYTES + r * 32);
-        const uint4 w0 = raw[0], w1 = raw[1];
+        if (leader && lane == 0) {
+          mbar_arrive_expect_tx(&bfull[st], S::B_BYTES);
+          tma_load_2d_nomc(a + S::A_BYTES, &tm_x, kk * BK, x0, &bfull[st]);
+        }
+        if (!wait_warp(&rfull[rs], (it / RSTAGES) & 1, abort_flag, status, 46)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* raw = rstage(rs);
+        const uint32_t p = reinterpret_cast<const uint32_t*>(raw + kRawBytes)[r];
+        const uint4 w0 = reinterpret_cast<const uint4*>(raw + r * 32)[0];
+        const uint4 w1 = reinterpret_cast<const uint4*>(raw + r * 32)[1];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[rs]);  // codes consumed: the slot may refill
+        const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
+        const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
         const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint8_t* row = a + r * 128;
 #pragma unroll
@@ -382,6 +422,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&afull[st]);
       }
       if (!ok) break;
+    }
+    if (warp == 6 && lane == 0) {  // activation tiles already requested land before exit
+      for (uint32_t j = it > STAGES ? it - STAGES : 0; j < it; ++j)
+        for (uint32_t p = 0; p < (1u << 20); ++p)
+          if (mbar_try_wait(&bfull[j % STAGES], (j / STAGES) & 1)) break;
     }
   }
   fence_before();
@@ -406,12 +451,13 @@ __global__ void w4_splitk_reduce(__nv_bfloat16* __restrict__ y, int64_t ldy,
   }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int RSTAGES>
 void launch(const CUtensorMap& tx, const uint8_t* qp, const uint32_t* sz, __nv_bfloat16* y,
             int64_t ldy, const __nv_bfloat16* bias, float* ws, int M, int N, int K, int Mpad,
             int group, int splits, int sms) {
-  using S = Smem<BN, STAGES>;
-  auto kern = gemm_w4a16_kernel<BN, STAGES>;
+  using S = Smem<BN, STAGES, RSTAGES>;
+  static_assert(S::BYTES <= 232448, "shared memory");
+  auto kern = gemm_w4a16_kernel<BN, STAGES, RSTAGES>;
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -450,7 +496,8 @@ int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::
   TORCH_CHECK(K % 8 == 0, "gemm_w4a16: K must be a multiple of 8 (16-byte TMA rows)");
   const int64_t ldx = x.dim() >= 2 ? x.stride(-2) : K;
   TORCH_CHECK(ldx % 8 == 0 && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 &&
-                  reinterpret_cast<uintptr_t>(qp.data_ptr()) % 16 == 0,
+                  reinterpret_cast<uintptr_t>(qp.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(sz.data_ptr()) % 16 == 0,
               "gemm_w4a16: 16-byte alignment");
   TORCH_CHECK(out.numel() / out.size(-1) == T && out.size(-1) >= M);
   if (T == 0) return 0;
@@ -491,11 +538,11 @@ int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::
   const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K),
             Mp = static_cast<int>(sz.size(1)), g = static_cast<int>(group);
   switch (bn) {
-    case 16: w4::launch<16, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 32: w4::launch<32, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 64: w4::launch<64, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 128: w4::launch<128, 5>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    default: w4::launch<256, 4>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 16: w4::launch<16, 6, 16>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 32: w4::launch<32, 6, 16>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 64: w4::launch<64, 6, 12>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 128: w4::launch<128, 5, 12>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    default: w4::launch<256, 4, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
   }
   if (splits > 1) {
     const int64_t n = M * T;

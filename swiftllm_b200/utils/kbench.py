@@ -6,6 +6,7 @@ single-shot runners used for ncu captures.
   python -m swiftllm_b200.utils.kbench prefill --shape 8,1024,32,8
   python -m swiftllm_b200.utils.kbench sweep [--json out.json]
   python -m swiftllm_b200.utils.kbench step --shape 256,700 [--model llama-2-7b] [--eager] [--once]
+  python -m swiftllm_b200.utils.kbench w4 [--shape 256x12288x4096,...] [--once]
 
 Timing rule: 3 warm-up runs, then each timed run reads a 256 MB buffer
 (larger than the 126 MB L2) before it, is bracketed by CUDA events on the
@@ -263,6 +264,33 @@ def fp8_case(T, N, K):
             "frac_bw": round(byts / t8 / 1e9 / (pk["hbm_gbs"] / 1e3), 3)}
 
 
+def w4_case(T, N, K, group=128, once=False):
+    """W4A16 int4 GEMM vs the library bf16 GEMM of the same shape (the
+    int4 weight moves a quarter of the bytes; the roofline is the bytes of
+    the int4 codes + scales + activations + output at the measured copy
+    bandwidth)."""
+    from ..ops import int4
+    C = cuda_ext()
+    x = torch.randn(T, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+    W = int4.quantize(w, group)
+    y = torch.empty(T, N, device="cuda", dtype=torch.bfloat16)
+    f4 = lambda: C.gemm_w4a16(y, x, W.qp, W.sz, N, group, None)  # noqa: E731
+    if once:
+        for _ in range(4):
+            f4()
+        torch.cuda.synchronize()
+        return None
+    t4 = _time(f4)
+    t16 = _time(lambda: torch.matmul(x, w.t(), out=y))
+    pk = measured_peaks()
+    byts = W.qp.numel() + W.sz.numel() * 4 + T * K * 2 + T * N * 2
+    return {"op": "gemm_w4a16", "T": T, "N": N, "K": K, "group": group, "w4_ms": round(t4, 4),
+            "cublas_bf16_ms": round(t16, 4), "w4_TB/s": round(byts / t4 / 1e9, 2),
+            "frac_bw": round(byts / t4 / 1e9 / (pk["hbm_gbs"] / 1e3), 3),
+            "w4_TFLOP/s": round(2.0 * T * N * K / t4 / 1e9, 1)}
+
+
 def sweep():
     res = []
     for T, N, K in [(256, 12288, 4096), (256, 4096, 4096), (256, 22016, 4096), (256, 4096, 11008),
@@ -281,7 +309,8 @@ def sweep():
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("op", choices=["gemm", "gemmchain", "decode", "prefill", "sweep", "step", "fp8"])
+    ap.add_argument("op", choices=["gemm", "gemmchain", "decode", "prefill", "sweep", "step", "fp8",
+                                       "w4"])
     ap.add_argument("--model", default="llama-2-7b")
     ap.add_argument("--eager", action="store_true")
     ap.add_argument("--shape", default=None)
@@ -300,6 +329,14 @@ def main(argv=None):
         for r in res:
             print(json.dumps(r), flush=True)
         res = None
+    elif a.op == "w4":
+        res = []
+        for c in (a.shape or "1x12288x4096,16x12288x4096,64x22016x4096,256x12288x4096,"
+                             "256x4096x11008,1024x12288x4096,8192x12288x4096").split(","):
+            r = w4_case(*[int(v) for v in c.split("x")], once=a.once)
+            if r:
+                print(json.dumps(r), flush=True)
+                res.append(r)
     else:
         shp = [int(v) for v in a.shape.split(",")]
         if a.op == "gemm":
