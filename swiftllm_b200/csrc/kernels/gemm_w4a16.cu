@@ -13,7 +13,7 @@
 //
 // Weight layout (built once at load by ops.int4): qp [ceil(M/128), ceil(K/64),
 // 128, 32] bytes, so the 128 x 64 int4 tile of one (feature tile, k step) is
-// one contiguous 4 KB block fetched by a single cp.async.bulk. Inside a row,
+// one contiguous 4 KB block fetched by one tensor-TMA box. Inside a row,
 // the 4 bytes of 16-byte output chunk c (K elements 8c .. 8c+7) form one
 // little-endian word whose nibble at bit 4j holds element 2j and the nibble at
 // bit 16 + 4j holds element 2j + 1 (j = 0..3); then
@@ -30,7 +30,7 @@
 //   activation tile). A codes slot is 1/4 of an operand slot, so the codes
 //   ring runs 6-16 k steps ahead and keeps enough bytes in flight per SM
 //   to stream the weights at HBM rate.
-//   warp 0      codes producer: two cp.async.bulk per k step;
+//   warp 0      codes producer: two tensor-TMA loads per k step;
 //   warp 1      TMEM allocation; one elected lane issues the MMAs;
 //               tcgen05.commit frees operand stages / publishes finished tiles;
 //   warps 2-5   epilogue: tcgen05.ld, bias, bf16 stores or fp32 split-K
@@ -185,8 +185,8 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 zb, __nv_bf
 // multiple of 64. ws: fp32 split-K partials [splits, N, M] when splits > 1.
 template <int BN, int STAGES, int RSTAGES>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_x, const uint8_t* __restrict__ qp,
-                      const uint32_t* __restrict__ sz, __nv_bfloat16* __restrict__ y, int64_t ldy,
+    gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
+                      const __grid_constant__ CUtensorMap tm_s, __nv_bfloat16* __restrict__ y, int64_t ldy,
                       const __nv_bfloat16* __restrict__ bias, float* __restrict__ ws, int M, int N,
                       int K, int Mpad, int group, int splits, int* status) {
   using S = Smem<BN, STAGES, RSTAGES>;
@@ -267,10 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* dst = rstage(r);
           mbar_arrive_expect_tx(&rfull[r], kRawBytes + kScBytes);
-          bulk_g2s(dst, qp + (size_t(m) * k_iters + kk) * kRawBytes, kRawBytes, &rfull[r]);
+          tma_load_2d_nomc(dst, &tm_q, 0, (m * k_iters + kk) * BM, &rfull[r]);
           // the 128 rows' (z, s) words of this k step's group: 512 contiguous bytes
-          bulk_g2s(dst + kRawBytes, sz + size_t((kk * BK) / group) * Mpad + m * BM, kScBytes,
-                   &rfull[r]);
+          tma_load_2d_nomc(dst + kRawBytes, &tm_s, m * BM, (kk * BK) / group, &rfull[r]);
         }
       }
       if (!ok) {  // let issued copies land before the CTA exits
@@ -451,8 +450,24 @@ __global__ void w4_splitk_reduce(__nv_bfloat16* __restrict__ y, int64_t ldy,
   }
 }
 
+// 2-D map without swizzle: [rows, cols] elements, row pitch in bytes, box
+// box_cols x box_rows.
+inline CUtensorMap make_tmap_plain(const void* ptr, CUtensorMapDataType dt, int64_t rows,
+                                   int64_t cols, int64_t pitch, int box_cols, int box_rows) {
+  CUtensorMap tm;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = tma_encode_fn()(&tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", static_cast<int>(r), ")");
+  return tm;
+}
+
 template <int BN, int STAGES, int RSTAGES>
-void launch(const CUtensorMap& tx, const uint8_t* qp, const uint32_t* sz, __nv_bfloat16* y,
+void launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, __nv_bfloat16* y,
             int64_t ldy, const __nv_bfloat16* bias, float* ws, int M, int N, int K, int Mpad,
             int group, int splits, int sms) {
   using S = Smem<BN, STAGES, RSTAGES>;
@@ -468,7 +483,7 @@ void launch(const CUtensorMap& tx, const uint8_t* qp, const uint32_t* sz, __nv_b
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   kern<<<std::min(tiles, sms), kThreads, S::BYTES, cur_stream()>>>(
-      tx, qp, sz, y, ldy, bias, ws, M, N, K, Mpad, group, splits, status_word_ptr());
+      tx, tq, ts, y, ldy, bias, ws, M, N, K, Mpad, group, splits, status_word_ptr());
   SWIFT_CHECK_LAUNCH();
 }
 
@@ -533,8 +548,13 @@ int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::
     ws = torch::empty({splits, T, M}, x.options().dtype(torch::kFloat));
     wsp = ws.data_ptr<float>();
   }
-  const uint8_t* q = qp.data_ptr<uint8_t>();
-  const uint32_t* s = reinterpret_cast<const uint32_t*>(sz.data_ptr<int32_t>());
+  // codes as a [Mt * Kt * 128, 32] byte matrix (one 128-row box = one 4 KB
+  // tile of a k step) and scales as [G, Mpad] u32 (one 128-word box = the
+  // (z, s) row of a group): both fetched by tensor TMA, no swizzle
+  const CUtensorMap q = w4::make_tmap_plain(qp.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, Mt * Kt * w4::BM,
+                                        32, 32, 32, w4::BM);
+  const CUtensorMap s = w4::make_tmap_plain(sz.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT32, sz.size(0),
+                                        sz.size(1), sz.size(1) * 4, w4::BM, 1);
   const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K),
             Mp = static_cast<int>(sz.size(1)), g = static_cast<int>(group);
   switch (bn) {
