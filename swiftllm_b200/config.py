@@ -42,6 +42,7 @@ class QuantizationMethod(Enum):
     FP8 = "fp8"
     INT8 = "int8"
     INT4 = "int4"
+    NVFP4 = "nvfp4"
 
 
 class SchedulerPolicy(Enum):

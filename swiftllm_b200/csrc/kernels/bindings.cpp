@@ -69,6 +69,8 @@ void spec_verify_greedy(torch::Tensor logits, torch::Tensor pos, torch::Tensor d
                         torch::Tensor temp, torch::Tensor out);
 int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
                    int64_t M, int64_t group, c10::optional<torch::Tensor> bias);
+int64_t gemm_nvfp4w(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sc,
+                    int64_t M, double gscale, c10::optional<torch::Tensor> bias);
 }  // namespace swift
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -116,6 +118,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &swift::moe_permute);
   m.def("moe_combine", &swift::moe_combine);
   m.def("gemm_w4a16", &swift::gemm_w4a16);
+  m.def("gemm_nvfp4w", &swift::gemm_nvfp4w);
   m.def("moe_gather", &swift::moe_gather);
   m.def("spec_verify_greedy", &swift::spec_verify_greedy);
 }

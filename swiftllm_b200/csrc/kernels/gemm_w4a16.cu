@@ -50,6 +50,8 @@
 
 #include <algorithm>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 #include "tma_util.cuh"
 
@@ -180,15 +182,42 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 zb, __nv_bf
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
+// NVFP4 codes: each nibble is E2M1 (bit 3 sign, bits 0-2 magnitude code
+// 0..7 = 0, 0.5, 1, 1.5, 2, 3, 4, 6), same nibble order as above. The bf16
+// bits of the magnitudes are looked up with byte permutes: high bytes
+// {00,3F,3F,3F,40,40,40,40}, low bytes {00,00,80,C0,00,40,80,C0}; the sign
+// bit moves to bit 15 / 31; one multiply by the block scale (a bf16 pair)
+// rounds once.
+__device__ __forceinline__ uint4 dequant8_fp4(uint32_t w, __nv_bfloat162 s) {
+  constexpr uint32_t kHi0 = 0x3F3F3F00u, kHi1 = 0x40404040u;
+  constexpr uint32_t kLo0 = 0xC0800000u, kLo1 = 0xC0804000u;
+  const uint32_t mag = w & 0x77777777u;
+  const uint32_t se = mag & 0xFFFFu, so = mag >> 16;  // elements 0,2,4,6 / 1,3,5,7
+  const uint32_t hiE = __byte_perm(kHi0, kHi1, se), loE = __byte_perm(kLo0, kLo1, se);
+  const uint32_t hiO = __byte_perm(kHi0, kHi1, so), loO = __byte_perm(kLo0, kLo1, so);
+  const uint32_t a0 = __byte_perm(loE, loO, 0x5140), b0 = __byte_perm(hiE, hiO, 0x5140);
+  const uint32_t a1 = __byte_perm(loE, loO, 0x7362), b1 = __byte_perm(hiE, hiO, 0x7362);
+  uint32_t o[4] = {__byte_perm(a0, b0, 0x5140), __byte_perm(a0, b0, 0x7362),
+                   __byte_perm(a1, b1, 0x5140), __byte_perm(a1, b1, 0x7362)};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    o[j] |= ((w >> (4 * j)) & 0x00080008u) << 12;
+    o[j] = bf2_as_u32(__hmul2(u32_as_bf2(o[j]), s));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
 // qp: packed int4 tiles; sz: [G, Mpad] (128 + z, s) bf16 pairs; group is a
 // multiple of 64. ws: fp32 split-K partials [splits, N, M] when splits > 1.
-template <int BN, int STAGES, int RSTAGES>
+// FMT 0: int4 codes with (128 + z, s) bf16 pairs per group; FMT 1: NVFP4
+// (E2M1 codes, four E4M3 block scales per row and k step in the scale word,
+// times the per-tensor gscale).
+template <int BN, int STAGES, int RSTAGES, int FMT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_q,
                       const __grid_constant__ CUtensorMap tm_s, __nv_bfloat16* __restrict__ y, int64_t ldy,
                       const __nv_bfloat16* __restrict__ bias, float* __restrict__ ws, int M, int N,
-                      int K, int Mpad, int group, int splits, int* status) {
+                      int K, int Mpad, int group, int splits, int* status, float gscale) {
   using S = Smem<BN, STAGES, RSTAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* tiles =
@@ -408,13 +437,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint4 w1 = reinterpret_cast<const uint4*>(raw + r * 32)[1];
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[rs]);  // codes consumed: the slot may refill
-        const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
-        const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
         const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         uint8_t* row = a + r * 128;
+        if constexpr (FMT == 0) {
+          const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
+          const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8(wv[c], zb, sc);
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8(wv[c], zb, sc);
+        } else {
+          __nv_bfloat162 sb[4];  // block b covers K elements 16b .. 16b + 15 (chunks 2b, 2b + 1)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const __half_raw h = __nv_cvt_fp8_to_halfraw(
+                static_cast<__nv_fp8_storage_t>((p >> (8 * b)) & 0xFFu), __NV_E4M3);
+            sb[b] = __float2bfloat162_rn(__half2float(__half(h)) * gscale);
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8_fp4(wv[c], sb[c >> 1]);
+        }
         // generic-proxy smem writes -> visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
@@ -466,13 +508,13 @@ inline CUtensorMap make_tmap_plain(const void* ptr, CUtensorMapDataType dt, int6
   return tm;
 }
 
-template <int BN, int STAGES, int RSTAGES>
+template <int BN, int STAGES, int RSTAGES, int FMT>
 void launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts, __nv_bfloat16* y,
             int64_t ldy, const __nv_bfloat16* bias, float* ws, int M, int N, int K, int Mpad,
-            int group, int splits, int sms) {
+            int group, int splits, int sms, float gscale) {
   using S = Smem<BN, STAGES, RSTAGES>;
   static_assert(S::BYTES <= 232448, "shared memory");
-  auto kern = gemm_w4a16_kernel<BN, STAGES, RSTAGES>;
+  auto kern = gemm_w4a16_kernel<BN, STAGES, RSTAGES, FMT>;
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -483,17 +525,17 @@ void launch(const CUtensorMap& tx, const CUtensorMap& tq, const CUtensorMap& ts,
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN) * splits;
   kern<<<std::min(tiles, sms), kThreads, S::BYTES, cur_stream()>>>(
-      tx, tq, ts, y, ldy, bias, ws, M, N, K, Mpad, group, splits, status_word_ptr());
+      tx, tq, ts, y, ldy, bias, ws, M, N, K, Mpad, group, splits, status_word_ptr(), gscale);
   SWIFT_CHECK_LAUNCH();
 }
 
 }  // namespace w4
 
-// out [T, M] bf16 = x [T, K] . dequant(qp, sz)^T (+ bias). qp uint8
-// [ceil(M/128), ceil(K/64), 128, 32] (tile-packed int4), sz int32 [G, Mpad]
-// ((128 + z, s) bf16 pairs), group a multiple of 64. Returns launches.
-int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
-                   int64_t M, int64_t group, c10::optional<torch::Tensor> bias) {
+// Shared host path of the two weight formats (checks, plan, launch).
+template <int FMT>
+static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
+                            int64_t M, int64_t group, c10::optional<torch::Tensor> bias,
+                            float gscale) {
   CHECK_BF16(x);
   CHECK_BF16(out);
   TORCH_CHECK(qp.scalar_type() == at::kByte && qp.is_contiguous() && qp.dim() == 4 &&
@@ -558,11 +600,11 @@ int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::
   const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K),
             Mp = static_cast<int>(sz.size(1)), g = static_cast<int>(group);
   switch (bn) {
-    case 16: w4::launch<16, 6, 16>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 32: w4::launch<32, 6, 16>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 64: w4::launch<64, 6, 12>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    case 128: w4::launch<128, 5, 12>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
-    default: w4::launch<256, 4, 6>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms); break;
+    case 16: w4::launch<16, 6, 16, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 32: w4::launch<32, 6, 16, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 64: w4::launch<64, 6, 12, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 128: w4::launch<128, 5, 12, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    default: w4::launch<256, 4, 6, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
   }
   if (splits > 1) {
     const int64_t n = M * T;
@@ -572,6 +614,22 @@ int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::
     return 2;
   }
   return 1;
+}
+
+// out [T, M] bf16 = x [T, K] . dequant(qp, sz)^T (+ bias). qp uint8
+// [ceil(M/128), ceil(K/64), 128, 32] (tile-packed int4), sz int32 [G, Mpad]
+// ((128 + z, s) bf16 pairs), group a multiple of 64. Returns launches.
+int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
+                   int64_t M, int64_t group, c10::optional<torch::Tensor> bias) {
+  return gemm_w4_impl<0>(out, x, qp, sz, M, group, bias, 1.f);
+}
+
+// NVFP4 weights: qp as above holding E2M1 codes, sc int32 [ceil(K/64), Mpad]
+// (four E4M3 block scales per row and k step, block b in byte b), gscale the
+// per-tensor fp32 scale. w = bf16(e2m1 * bf16(e4m3 * gscale)).
+int64_t gemm_nvfp4w(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sc,
+                    int64_t M, double gscale, c10::optional<torch::Tensor> bias) {
+  return gemm_w4_impl<1>(out, x, qp, sc, M, 64, bias, static_cast<float>(gscale));
 }
 
 }  // namespace swift

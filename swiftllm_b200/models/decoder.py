@@ -192,6 +192,9 @@ class DecoderModel:
                 elif isinstance(v, ops.Int4Weight):
                     yield f"layers.{i}.{k}.qp", v.qp
                     yield f"layers.{i}.{k}.sz", v.sz
+                elif isinstance(v, ops.Nvfp4Weight):
+                    yield f"layers.{i}.{k}.qp", v.qp
+                    yield f"layers.{i}.{k}.sc", v.sc
                 elif isinstance(v, torch.Tensor):
                     yield f"layers.{i}.{k}", v
         yield "norm", self.norm_w
@@ -284,6 +287,19 @@ class DecoderModel:
                 if isinstance(w, torch.Tensor) and w.dim() == 2:
                     g = -(-w.shape[1] // 64) * 64 if group <= 0 else -(-group // 64) * 64
                     setattr(L, name, ops.int4.quantize(w, g))
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+
+    def quantize_nvfp4(self) -> None:
+        """NVFP4 weight storage for the dense projections (QKV, o_proj,
+        gate_up / fc1, down / fc2): E2M1 codes with an E4M3 scale per 16
+        input features and a per-tensor scale, expanded to bf16 in shared
+        memory by the GEMM. Activations stay bf16."""
+        for L in self.layers:
+            for name in ("wqkv", "wo", "w13", "w1", "w2"):
+                w = getattr(L, name, None)
+                if isinstance(w, torch.Tensor) and w.dim() == 2:
+                    setattr(L, name, ops.int4.quantize_nvfp4(w))
         if self.device.type == "cuda":
             torch.cuda.empty_cache()
 

@@ -144,7 +144,7 @@ class Int8Weight:
 
 
 from . import int4  # noqa: E402
-from .int4 import Int4Weight  # noqa: E402
+from .int4 import Int4Weight, Nvfp4Weight  # noqa: E402
 
 
 def quantize_s8(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -237,6 +237,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, b: Optional[torch.Tensor] = None,
         return _linear_int8(x, w, b, out)
     if isinstance(w, Int4Weight):
         return int4.linear(x, w, b, out)
+    if isinstance(w, Nvfp4Weight):
+        return int4.linear_nvfp4(x, w, b, out)
     if not x.is_cuda:
         return ref.linear(x, w, b)
     if _GEMM_BACKEND == "cublas" or (_GEMM_BACKEND == "auto" and _library_faster(x, w)):

@@ -224,3 +224,95 @@ def linear(x: torch.Tensor, w: Int4Weight, b: Optional[torch.Tensor] = None,
         out = torch.empty(x.shape[:-1] + (w.M,), dtype=x.dtype, device=x.device)
     _count(cuda_ext().gemm_w4a16(out, x, w.qp, w.sz, w.M, w.group, b))
     return out
+
+
+# ---------------------------------------------------------------- NVFP4
+# E2M1 magnitudes by 3-bit code; bit 3 of a nibble is the sign.
+E2M1 = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+class Nvfp4Weight:
+    """A linear weight [M, K] in NVFP4: E2M1 codes, one E4M3 scale per 16
+    input features, one fp32 scale per tensor; w = bf16(e2m1 * bf16(e4m3 *
+    gscale)). The kernel multiplies in bf16 on the tensor cores (the codes are
+    a storage format: a quarter of the bf16 weight bytes plus 1/16 for the
+    block scales).
+
+    qp: uint8 [ceil(M/128), ceil(K/64), 128, 32] (same packing as int4)
+    sc: int32 [ceil(K/64), ceil(M/128)*128], byte b = E4M3 scale of block b
+    """
+
+    def __init__(self, qp: torch.Tensor, sc: torch.Tensor, gscale: float, M: int, K: int):
+        self.qp, self.sc, self.gscale, self.M, self.K = qp, sc, float(gscale), M, K
+
+    @property
+    def shape(self):
+        return (self.M, self.K)
+
+    @property
+    def device(self):
+        return self.qp.device
+
+    def block_scales(self) -> torch.Tensor:
+        """[M, ceil(K/16)] fp32 effective block scales bf16(e4m3 * gscale)."""
+        b = self.sc.contiguous().view(torch.uint8).reshape(self.sc.shape[0], -1, 4)  # [Kt, Mpad, 4]
+        e4 = b.view(torch.float8_e4m3fn).float().permute(1, 0, 2).reshape(b.shape[1], -1)
+        return (e4 * self.gscale).to(torch.bfloat16).float()[: self.M]
+
+    def dequantize(self) -> torch.Tensor:
+        """[M, K] fp32 holding exactly the bf16 values the kernel multiplies."""
+        q = Int4Weight(self.qp, torch.zeros(1, self.qp.shape[0] * BM, dtype=torch.int32,
+                                             device=self.qp.device), self.M, self.K, BK).codes()[0]
+        lut = torch.tensor(E2M1, device=q.device)
+        v = lut[(q & 7).long()] * torch.where((q & 8) > 0, -1.0, 1.0)
+        s = self.block_scales()[:, torch.arange(self.K, device=q.device) // 16]
+        return (v * s).to(torch.bfloat16).float()
+
+
+def quantize_nvfp4(w: torch.Tensor) -> Nvfp4Weight:
+    """NVFP4 quantisation of w [M, K]: gscale = amax(w) / (448 * 6); per block
+    of 16 input features the E4M3 scale rounds amax(block) / 6 / gscale; each
+    element takes the nearest E2M1 value of w / bf16(e4m3 * gscale) (ties to
+    the smaller magnitude)."""
+    M, K = w.shape
+    Kt = math.ceil(K / BK)
+    Mt = math.ceil(M / BM)
+    wf = torch.zeros(M, Kt * BK, dtype=torch.float32, device=w.device)
+    wf[:, :K] = w.float()
+    blocks = wf.view(M, Kt * 4, 16)
+    amax = blocks.abs().amax(-1)
+    gscale = max(float(amax.max()) / (448.0 * 6.0), 1e-30)
+    e4 = (amax / 6.0 / gscale).clamp(max=448.0).to(torch.float8_e4m3fn)
+    eff = (e4.float() * gscale).to(torch.bfloat16).float()
+    x = blocks / eff.clamp_min(1e-30)[..., None]
+    grid = torch.tensor(E2M1, device=w.device)
+    mag = (x.abs()[..., None] - grid).abs().argmin(-1)  # nearest, first on ties
+    code = (mag | torch.where(x < 0, 8, 0)).to(torch.uint8).view(M, Kt * BK)
+    qp = pack(code, torch.zeros(1, M), torch.zeros(1, M), BK).qp
+    scb = torch.zeros(Mt * BM, Kt * 4, dtype=torch.uint8, device=w.device)
+    scb[:M] = e4.view(torch.uint8)
+    sc = scb.view(Mt * BM, Kt, 4).permute(1, 0, 2).contiguous().view(torch.int32).view(Kt, Mt * BM)
+    return Nvfp4Weight(qp, sc, gscale, M, K)
+
+
+def linear_nvfp4(x: torch.Tensor, w: Nvfp4Weight, b: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x [..., K] . dequant(w)^T (+ b): the tcgen05 kernel on CUDA, the
+    dequantised fp32 maths on CPU."""
+    from . import _count, cuda_ext
+    if not x.is_cuda:
+        y = x.float() @ w.dequantize().t()
+        if b is not None:
+            y = y + b.float()
+        y = y.to(x.dtype).reshape(x.shape[:-1] + (w.M,))
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    K = x.shape[-1]
+    if K % 8:
+        x = torch.nn.functional.pad(x, (0, 8 - K % 8))
+    if out is None:
+        out = torch.empty(x.shape[:-1] + (w.M,), dtype=x.dtype, device=x.device)
+    _count(cuda_ext().gemm_nvfp4w(out, x, w.qp, w.sc, w.M, w.gscale, b))
+    return out

@@ -154,9 +154,11 @@ class ModelRunner:
             self.model.quantize_int8()
         elif q in ("int4", "gptq", "awq"):
             self.model.quantize_int4(group)
+        elif q == "nvfp4":
+            self.model.quantize_nvfp4()
         elif q not in (None, "none"):
             raise NotImplementedError(f"quantization {q!r} is not supported "
-                                      "(fp8, int8, int4 / gptq / awq are)")
+                                      "(fp8, int8, int4 / gptq / awq, nvfp4 are)")
         elif (self.is_cuda and ops.gemm_backend() == "tcgen05"
               and os.environ.get("SWIFTLLM_FUSE_SWIGLU", "1") != "0"):
             # our GEMMs everywhere: SwiGLU in the gate/up GEMM epilogue

@@ -171,3 +171,60 @@ def test_gptq_checkpoint_loads_same_codes(tmp_path):
             quantization="int4")
     ob = b.generate(prompt_token_ids=prompts, sampling_params=sp, use_tqdm=False)
     assert [o.outputs[0].token_ids for o in oa] == [o.outputs[0].token_ids for o in ob]
+
+
+def _byte_perm(a, b, s):
+    """CUDA __byte_perm: result byte n = byte (s >> 4n) & 7 of (b:a)."""
+    src = (b.astype(np.uint64) << np.uint64(32)) | a.astype(np.uint64)
+    out = np.zeros_like(a, dtype=np.uint64)
+    for n in range(4):
+        sel = (np.asarray(s, dtype=np.uint64) >> np.uint64(4 * n)) & np.uint64(7)
+        out |= ((src >> (sel * np.uint64(8))) & np.uint64(0xFF)) << np.uint64(8 * n)
+    return out.astype(np.uint32)
+
+
+def _fp4_kernel_emulation(W) -> torch.Tensor:
+    """The kernel's E2M1 decode (byte-permute tables, sign move) times the
+    bf16 block scale, rounded to bf16 like the bf16x2 multiply."""
+    Mt, Kt = W.qp.shape[:2]
+    words = W.qp.permute(0, 2, 1, 3).reshape(Mt * 128, Kt * 8, 4).numpy().view(np.uint32)[..., 0]
+    c = lambda v: np.full(words.shape, v, np.uint32)  # noqa: E731
+    mag = words & np.uint32(0x77777777)
+    se, so = mag & np.uint32(0xFFFF), mag >> np.uint32(16)
+    hiE, loE = _byte_perm(c(0x3F3F3F00), c(0x40404040), se), _byte_perm(c(0xC0800000), c(0xC0804000), se)
+    hiO, loO = _byte_perm(c(0x3F3F3F00), c(0x40404040), so), _byte_perm(c(0xC0800000), c(0xC0804000), so)
+    a0, b0 = _byte_perm(loE, loO, 0x5140), _byte_perm(hiE, hiO, 0x5140)
+    a1, b1 = _byte_perm(loE, loO, 0x7362), _byte_perm(hiE, hiO, 0x7362)
+    o = [_byte_perm(a0, b0, 0x5140), _byte_perm(a0, b0, 0x7362),
+         _byte_perm(a1, b1, 0x5140), _byte_perm(a1, b1, 0x7362)]
+    scale = W.block_scales().numpy()  # [M, Kt*4]
+    out = np.zeros((Mt * 128, Kt * 64), np.float32)
+    for j in range(4):
+        oj = o[j] | (((words >> np.uint32(4 * j)) & np.uint32(0x00080008)) << np.uint32(12))
+        for half, v in ((0, _bf16_bits_to_float((oj & 0xFFFF).astype(np.uint16))),
+                        (1, _bf16_bits_to_float((oj >> 16).astype(np.uint16)))):
+            cols = np.arange(Kt * 8) * 8 + 2 * j + half
+            sc = np.zeros((Mt * 128, cols.size), np.float32)
+            sc[: W.M] = scale[:, cols // 16]
+            out[:, cols] = torch.from_numpy(v * sc).to(torch.bfloat16).float().numpy()
+    return torch.from_numpy(out[: W.M, : W.K])
+
+
+@pytest.mark.parametrize("M,K", [(200, 300), (128, 64)])
+def test_nvfp4_layout_matches_kernel_emulation(M, K):
+    torch.manual_seed(M + K)
+    w = torch.randn(M, K) * 0.05
+    W = int4.quantize_nvfp4(w)
+    assert torch.equal(_fp4_kernel_emulation(W), W.dequantize())
+    # every element within half an E2M1 step (<= 1 unit of its block scale)
+    s = W.block_scales()[:, torch.arange(K) // 16]
+    assert ((W.dequantize() - w).abs() <= s * 1.0 + 0.01 * w.abs() + 1e-6).all()
+
+
+def test_nvfp4_model_generates():
+    sp = SamplingParams(temperature=0, max_tokens=6, ignore_eos=True)
+    a = LLM("tiny-llama", load_format="dummy", device="cpu", dtype="float32", max_model_len=128,
+            quantization="nvfp4")
+    out = a.generate(prompt_token_ids=[[5, 6, 7, 8]], sampling_params=sp, use_tqdm=False)
+    assert isinstance(a.llm_engine.executor.runner.model.layers[0].wqkv, ops.Nvfp4Weight)
+    assert len(out[0].outputs[0].token_ids) == 6

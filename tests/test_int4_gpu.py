@@ -63,3 +63,31 @@ def test_int4_model_gpu():
     st = ops.cuda_ext().read_status(True)
     assert st[0] == 0, st
     llm.shutdown()
+
+
+@pytest.mark.parametrize("T,M,K", [(1, 4096, 4096), (37, 200, 328), (300, 1000, 1024),
+                                   (5, 4096, 11008)])
+def test_gemm_nvfp4w(C, T, M, K):
+    # NVFP4 weights (E2M1 codes, E4M3 block scales, per-tensor scale) expanded
+    # to bf16 in shared memory: against the fp32 product of the same weights
+    from swiftllm_b200.ops import int4
+    torch.manual_seed(T + M)
+    x = (torch.randn(T, K, device="cuda") * 0.5).to(torch.bfloat16)
+    W = int4.quantize_nvfp4(torch.randn(M, K, device="cuda") * 0.05)
+    out = torch.empty(T, M, dtype=torch.bfloat16, device="cuda")
+    C.gemm_nvfp4w(out, x, W.qp, W.sc, M, W.gscale, None)
+    r = x.float() @ W.dequantize().t()
+    torch.testing.assert_close(out.float(), r, rtol=1e-2, atol=1e-2)
+    st = C.read_status(True)
+    assert st[0] == 0, st
+
+
+def test_nvfp4_model_gpu():
+    from swiftllm_b200 import LLM, SamplingParams, ops
+    sp = SamplingParams(temperature=0, max_tokens=8, ignore_eos=True)
+    llm = LLM("tiny-llama", load_format="dummy", dtype="bfloat16", gpu_memory_utilization=0.3,
+              max_model_len=256, quantization="nvfp4")
+    out = llm.generate(prompt_token_ids=[list(range(100, 140))], sampling_params=sp, use_tqdm=False)
+    assert len(out[0].outputs[0].token_ids) == 8
+    assert isinstance(llm.llm_engine.executor.runner.model.layers[0].wqkv, ops.Nvfp4Weight)
+    llm.shutdown()
