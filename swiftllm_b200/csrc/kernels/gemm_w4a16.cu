@@ -11,9 +11,10 @@
 // next to the tensor cores, and the MMA itself is the plain bf16
 // tcgen05.mma.kind::f16 with fp32 accumulators in TMEM.
 //
-// Weight layout (built once at load by ops.int4): qp [ceil(M/128), ceil(K/64),
-// 128, 32] bytes, so the 128 x 64 int4 tile of one (feature tile, k step) is
-// one contiguous 4 KB block fetched by one tensor-TMA box. Inside a row,
+// Weight layout (built once at load by ops.int4): qp [ceil(M/128), 2*ceil(K/128),
+// 128, 32] bytes: the 128 x 64 code tile of one (feature tile, 64-wide K
+// slice) is one contiguous 4 KB block, and a k step (128 of K) fetches two
+// consecutive tiles with one 256-row tensor-TMA box. Inside a row,
 // the 4 bytes of 16-byte output chunk c (K elements 8c .. 8c+7) form one
 // little-endian word whose nibble at bit 4j holds element 2j and the nibble at
 // bit 16 + 4j holds element 2j + 1 (j = 0..3); then
@@ -23,27 +24,27 @@
 // (pair - (128 + z)) is exact in bf16 and the multiply by s rounds once, so
 // each dequantised weight equals bf16((q - z) * s) exactly.
 //
-// CTA (22 warps, one per SM, persistent over output tiles), two rings:
-//   codes ring (RSTAGES slots of 4.5 KB: the 4 KB int4 tile of one k step
-//   and the 512-byte (z, s) row of its group) and operand ring (STAGES
-//   slots: the bf16 A tile the dequantisation writes and the BN x 64
-//   activation tile). A codes slot is 1/4 of an operand slot, so the codes
-//   ring runs 6-16 k steps ahead and keeps enough bytes in flight per SM
-//   to stream the weights at HBM rate.
-//   warp 0      codes producer: two tensor-TMA loads per k step;
-//   warp 1      TMEM allocation; one elected lane issues the MMAs;
-//               tcgen05.commit frees operand stages / publishes finished tiles;
+// CTA (14 warps, one per SM, persistent over output tiles), two rings:
+//   codes ring (RSTAGES slots of 9 KB: the two 4 KB code tiles of one k step
+//   and the 512-byte scale row of each tile's group) and operand ring
+//   (STAGES slots: two 128 x 64 bf16 A sub-tiles the dequantisation writes
+//   and the two BN x 64 activation sub-tiles). The codes ring runs several
+//   k steps ahead of the dequantisation.
+//   warp 0      codes producer: three tensor-TMA loads per k step;
+//   warp 1      TMEM allocation; one elected lane issues the eight MMAs of a
+//               k step; tcgen05.commit frees operand stages / publishes
+//               finished tiles;
 //   warps 2-5   epilogue: tcgen05.ld, bias, bf16 stores or fp32 split-K
 //               partials; two TMEM accumulators overlap tile i's epilogue
 //               with tile i+1's MMAs;
-//   warps 6-21  dequantisation, 4 groups of 4 warps taking k steps round
-//               robin: wait for the operand stage to be free (the group's
-//               first warp then requests its activation tile by 2-D TMA,
+//   warps 6-13  dequantisation, 2 groups of 4 warps taking k steps in turn:
+//               wait for the operand stage to be free (the group's first
+//               warp then requests its activation sub-tiles by 2-D TMA,
 //               128-byte swizzle, no multicast), read the codes (freeing the
-//               codes slot), one thread per weight row expands 64 nibbles
-//               into the K-major 128-byte-swizzled bf16 A tile (chunk c of
-//               row r stored at chunk c ^ (r & 7)), then fence.proxy.async
-//               so the tensor core sees the writes.
+//               codes slot), one thread per weight row expands 2 x 64
+//               nibbles into the K-major 128-byte-swizzled bf16 A sub-tiles
+//               (chunk c of row r stored at chunk c ^ (r & 7)), then
+//               fence.proxy.async so the tensor core sees the writes.
 // Every mbarrier wait is bounded (status word + CTA abort flag; in-flight
 // copies and MMAs are drained and TMEM freed before the CTA returns).
 #include <cudaTypedefs.h>
@@ -58,18 +59,21 @@
 namespace swift {
 namespace w4 {
 
-constexpr int BM = 128, BK = 64;
-constexpr int kDqGroups = 4;                     // dequantisation groups of 4 warps
-constexpr int kThreads = (6 + 4 * kDqGroups) * 32;  // 704
-constexpr int kRawBytes = BM * BK / 2;  // 4 KB of int4 per stage
-constexpr int kScBytes = BM * 4;        // (128 + z, s) of the stage's 128 rows
+constexpr int BM = 128, BK = 64;               // one packed code tile: 128 rows x 64 K
+constexpr int KSUB = 2, KSTEP = BK * KSUB;      // a k step covers two code tiles (128 K)
+constexpr int kDqGroups = 2;                     // dequantisation groups of 4 warps
+constexpr int kThreads = (6 + 4 * kDqGroups) * 32;  // 448
+constexpr int kRawBytes = KSUB * BM * BK / 2;   // 8 KB of codes per k step
+constexpr int kScBytes = KSUB * BM * 4;         // a scale word per row and code tile
 constexpr int kRawRegion = kRawBytes + kScBytes;  // one codes-ring slot
 constexpr uint32_t kWaitLimit = 1u << 25;
 
 template <int BN, int STAGES, int RSTAGES>
 struct Smem {
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_SUB = BM * BK * 2;   // one 128 x 64 bf16 swizzled sub-tile
+  static constexpr int B_SUB = BN * BK * 2;
+  static constexpr int A_BYTES = KSUB * A_SUB;
+  static constexpr int B_BYTES = KSUB * B_SUB;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // bf16 operands of one k step
   static constexpr int TMEM_COLS = (2 * BN) <= 32    ? 32
                                    : (2 * BN) <= 64  ? 64
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m_tiles = (M + BM - 1) / BM;
   const int n_tiles = (N + BN - 1) / BN;
-  const int k_iters = (K + BK - 1) / BK;
+  const int k_iters = (K + KSTEP - 1) / KSTEP;  // code tiles per feature tile: KSUB * k_iters
   const int k_per = (k_iters + splits - 1) / splits;
   const int total = m_tiles * n_tiles * splits;
 
@@ -296,9 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* dst = rstage(r);
           mbar_arrive_expect_tx(&rfull[r], kRawBytes + kScBytes);
-          tma_load_2d_nomc(dst, &tm_q, 0, (m * k_iters + kk) * BM, &rfull[r]);
-          // the 128 rows' (z, s) words of this k step's group: 512 contiguous bytes
-          tma_load_2d_nomc(dst + kRawBytes, &tm_s, m * BM, (kk * BK) / group, &rfull[r]);
+          // two consecutive code tiles (one 256-row box) and the scale row of
+          // each tile's group
+          tma_load_2d_nomc(dst, &tm_q, 0, (m * k_iters + kk) * KSUB * BM, &rfull[r]);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub)
+            tma_load_2d_nomc(dst + kRawBytes + sub * BM * 4, &tm_s, m * BM,
+                             (kk * KSTEP + sub * BK) / group, &rfull[r]);
         }
       }
       if (!ok) {  // let issued copies land before the CTA exits
@@ -333,10 +341,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_after();
         if (elect()) {
           const uint8_t* a = stage(st);
-          const uint64_t ad = desc_sw128(a), bd = desc_sw128(a + S::A_BYTES);
 #pragma unroll
-          for (int j = 0; j < BK / 16; ++j)  // +32 B along K inside the swizzle atom
-            mma(d_tmem, ad + 2 * j, bd + 2 * j, id, (kk > k0 || j > 0) ? 1u : 0u);
+          for (int j = 0; j < KSTEP / 16; ++j) {  // sub-tile j / 4, +32 B along K inside its atom
+            const int sub = j / (BK / 16), jj = j % (BK / 16);
+            const uint64_t ad = desc_sw128(a + sub * S::A_SUB);
+            const uint64_t bd = desc_sw128(a + S::A_BYTES + sub * S::B_SUB);
+            mma(d_tmem, ad + 2 * jj, bd + 2 * jj, id, (kk > k0 || j > 0) ? 1u : 0u);
+          }
           commit(&abempty[st]);
         }
         __syncwarp();
@@ -425,37 +436,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* a = stage(st);
         if (leader && lane == 0) {
           mbar_arrive_expect_tx(&bfull[st], S::B_BYTES);
-          tma_load_2d_nomc(a + S::A_BYTES, &tm_x, kk * BK, x0, &bfull[st]);
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub)
+            tma_load_2d_nomc(a + S::A_BYTES + sub * S::B_SUB, &tm_x, kk * KSTEP + sub * BK, x0,
+                             &bfull[st]);
         }
         if (!wait_warp(&rfull[rs], (it / RSTAGES) & 1, abort_flag, status, 46)) {
           ok = false;
           break;
         }
         const uint8_t* raw = rstage(rs);
-        const uint32_t p = reinterpret_cast<const uint32_t*>(raw + kRawBytes)[r];
-        const uint4 w0 = reinterpret_cast<const uint4*>(raw + r * 32)[0];
-        const uint4 w1 = reinterpret_cast<const uint4*>(raw + r * 32)[1];
+        uint32_t p[KSUB];
+        uint32_t wv[KSUB][8];
+#pragma unroll
+        for (int sub = 0; sub < KSUB; ++sub) {
+          p[sub] = reinterpret_cast<const uint32_t*>(raw + kRawBytes + sub * BM * 4)[r];
+          const uint4 w0 = reinterpret_cast<const uint4*>(raw + (sub * BM + r) * 32)[0];
+          const uint4 w1 = reinterpret_cast<const uint4*>(raw + (sub * BM + r) * 32)[1];
+          wv[sub][0] = w0.x; wv[sub][1] = w0.y; wv[sub][2] = w0.z; wv[sub][3] = w0.w;
+          wv[sub][4] = w1.x; wv[sub][5] = w1.y; wv[sub][6] = w1.z; wv[sub][7] = w1.w;
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&rempty[rs]);  // codes consumed: the slot may refill
-        const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint8_t* row = a + r * 128;
-        if constexpr (FMT == 0) {
-          const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p).x);
-          const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p).y);
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8(wv[c], zb, sc);
-        } else {
-          __nv_bfloat162 sb[4];  // block b covers K elements 16b .. 16b + 15 (chunks 2b, 2b + 1)
+        for (int sub = 0; sub < KSUB; ++sub) {
+          uint8_t* row = a + sub * S::A_SUB + r * 128;
+          if constexpr (FMT == 0) {
+            const __nv_bfloat162 zb = __bfloat162bfloat162(u32_as_bf2(p[sub]).x);
+            const __nv_bfloat162 sc = __bfloat162bfloat162(u32_as_bf2(p[sub]).y);
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const __half_raw h = __nv_cvt_fp8_to_halfraw(
-                static_cast<__nv_fp8_storage_t>((p >> (8 * b)) & 0xFFu), __NV_E4M3);
-            sb[b] = __float2bfloat162_rn(__half2float(__half(h)) * gscale);
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8(wv[sub][c], zb, sc);
+          } else {
+            __nv_bfloat162 sb[4];  // block b covers K elements 16b .. 16b + 15 (chunks 2b, 2b + 1)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const __half_raw h = __nv_cvt_fp8_to_halfraw(
+                  static_cast<__nv_fp8_storage_t>((p[sub] >> (8 * b)) & 0xFFu), __NV_E4M3);
+              sb[b] = __float2bfloat162_rn(__half2float(__half(h)) * gscale);
+            }
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) =
+                  dequant8_fp4(wv[sub][c], sb[c >> 1]);
           }
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = dequant8_fp4(wv[c], sb[c >> 1]);
         }
         // generic-proxy smem writes -> visible to the tensor core (async proxy)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -545,8 +569,10 @@ static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp
               "gemm_w4a16: sz must be int32 [G, Mpad]");
   TORCH_CHECK(group > 0 && group % w4::BK == 0, "gemm_w4a16: group must be a multiple of 64");
   const int64_t K = x.size(-1), T = x.numel() / K;
-  const int64_t Mt = (M + w4::BM - 1) / w4::BM, Kt = (K + w4::BK - 1) / w4::BK;
-  TORCH_CHECK(qp.size(0) == Mt && qp.size(1) == Kt, "gemm_w4a16: qp tiles do not match M, K");
+  const int64_t Mt = (M + w4::BM - 1) / w4::BM;
+  const int64_t Kt = w4::KSUB * ((K + w4::KSTEP - 1) / w4::KSTEP);  // code tiles, even
+  TORCH_CHECK(qp.size(0) == Mt && qp.size(1) == Kt,
+              "gemm_w4a16: qp must hold [ceil(M/128), 2*ceil(K/128)] code tiles");
   TORCH_CHECK(sz.size(1) == Mt * w4::BM && sz.size(0) >= (Kt * w4::BK + group - 1) / group,
               "gemm_w4a16: sz shape");
   TORCH_CHECK(x.stride(-1) == 1 && out.stride(-1) == 1, "gemm_w4a16: inner dims contiguous");
@@ -578,7 +604,7 @@ static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp
   const int64_t tiles = Mt * ((T + bn - 1) / bn);
   int splits = 1;
   if (tiles < sms * 3 / 4)
-    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, Kt / 4, 8})));
+    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, Kt / 8, 8})));
   CUtensorMap tx = make_tmap_2d(x.data_ptr(), T, K, ldx, w4::BK, bn);
   auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   const __nv_bfloat16* bp =
@@ -594,17 +620,17 @@ static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp
   // tile of a k step) and scales as [G, Mpad] u32 (one 128-word box = the
   // (z, s) row of a group): both fetched by tensor TMA, no swizzle
   const CUtensorMap q = w4::make_tmap_plain(qp.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, Mt * Kt * w4::BM,
-                                        32, 32, 32, w4::BM);
+                                        32, 32, 32, w4::KSUB * w4::BM);
   const CUtensorMap s = w4::make_tmap_plain(sz.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT32, sz.size(0),
                                         sz.size(1), sz.size(1) * 4, w4::BM, 1);
   const int Mi = static_cast<int>(M), Ni = static_cast<int>(T), Ki = static_cast<int>(K),
             Mp = static_cast<int>(sz.size(1)), g = static_cast<int>(group);
   switch (bn) {
-    case 16: w4::launch<16, 6, 16, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
-    case 32: w4::launch<32, 6, 16, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
-    case 64: w4::launch<64, 6, 12, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
-    case 128: w4::launch<128, 5, 12, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
-    default: w4::launch<256, 4, 6, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 16: w4::launch<16, 4, 8, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 32: w4::launch<32, 3, 10, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 64: w4::launch<64, 3, 8, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    case 128: w4::launch<128, 2, 10, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
+    default: w4::launch<256, 2, 3, FMT>(tx, q, s, y, ldy, bp, wsp, Mi, Ni, Ki, Mp, g, splits, sms, gscale); break;
   }
   if (splits > 1) {
     const int64_t n = M * T;
@@ -617,14 +643,14 @@ static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp
 }
 
 // out [T, M] bf16 = x [T, K] . dequant(qp, sz)^T (+ bias). qp uint8
-// [ceil(M/128), ceil(K/64), 128, 32] (tile-packed int4), sz int32 [G, Mpad]
+// [ceil(M/128), 2*ceil(K/128), 128, 32] (tile-packed int4), sz int32 [G, Mpad]
 // ((128 + z, s) bf16 pairs), group a multiple of 64. Returns launches.
 int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
                    int64_t M, int64_t group, c10::optional<torch::Tensor> bias) {
   return gemm_w4_impl<0>(out, x, qp, sz, M, group, bias, 1.f);
 }
 
-// NVFP4 weights: qp as above holding E2M1 codes, sc int32 [ceil(K/64), Mpad]
+// NVFP4 weights: qp as above holding E2M1 codes, sc int32 [2*ceil(K/128), Mpad]
 // (four E4M3 block scales per row and k step, block b in byte b), gscale the
 // per-tensor fp32 scale. w = bf16(e2m1 * bf16(e4m3 * gscale)).
 int64_t gemm_nvfp4w(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sc,

@@ -29,11 +29,17 @@ _KPERM = (0, 2, 4, 6, 1, 3, 5, 7)
 _AWQ_ORDER = (0, 2, 4, 6, 1, 3, 5, 7)
 
 
+def _code_tiles(K: int) -> int:
+    """64-wide code tiles along K: an even count, since the kernel's k step
+    reads two consecutive tiles (128 input features)."""
+    return 2 * math.ceil(K / (2 * BK))
+
+
 class Int4Weight:
     """A linear weight [M, K] as int4 codes with per-(group, feature) scale
     and zero point.
 
-    qp: uint8 [ceil(M/128), ceil(K/64), 128, 32] (tile-packed codes)
+    qp: uint8 [ceil(M/128), 2*ceil(K/128), 128, 32] (tile-packed codes)
     sz: int32 [G, ceil(M/128)*128], each word the bf16 pair (128 + z, s)
     """
 
@@ -59,8 +65,9 @@ class Int4Weight:
             q[..., e] = nib[..., pos]
         q = q.reshape(Mt * BM, Kt * BK)[: self.M, : self.K].to(torch.uint8)
         pair = self.sz.view(torch.int16).reshape(self.sz.shape[0], -1, 2)
-        zb = pair[..., 0].view(torch.bfloat16).float()[:, : self.M]
-        s = pair[..., 1].view(torch.bfloat16).float()[:, : self.M]
+        G = math.ceil(self.K / self.group)
+        zb = pair[:G, :, 0].view(torch.bfloat16).float()[:, : self.M]
+        s = pair[:G, :, 1].view(torch.bfloat16).float()[:, : self.M]
         return q, zb - 128.0, s
 
     def dequantize(self) -> torch.Tensor:
@@ -78,7 +85,7 @@ def pack(q: torch.Tensor, z: torch.Tensor, s: torch.Tensor, group: int) -> Int4W
     if group % BK:
         raise ValueError(f"int4 group size must be a multiple of {BK}, got {group}")
     M, K = q.shape
-    Mt, Kt = math.ceil(M / BM), math.ceil(K / BK)
+    Mt, Kt = math.ceil(M / BM), _code_tiles(K)
     G = math.ceil(Kt * BK / group)
     dev = q.device
     qpad = torch.zeros(Mt * BM, Kt * BK, dtype=torch.uint8, device=dev)
@@ -238,8 +245,8 @@ class Nvfp4Weight:
     a storage format: a quarter of the bf16 weight bytes plus 1/16 for the
     block scales).
 
-    qp: uint8 [ceil(M/128), ceil(K/64), 128, 32] (same packing as int4)
-    sc: int32 [ceil(K/64), ceil(M/128)*128], byte b = E4M3 scale of block b
+    qp: uint8 [ceil(M/128), 2*ceil(K/128), 128, 32] (same packing as int4)
+    sc: int32 [2*ceil(K/128), ceil(M/128)*128], byte b = E4M3 scale of block b
     """
 
     def __init__(self, qp: torch.Tensor, sc: torch.Tensor, gscale: float, M: int, K: int):
@@ -275,7 +282,7 @@ def quantize_nvfp4(w: torch.Tensor) -> Nvfp4Weight:
     element takes the nearest E2M1 value of w / bf16(e4m3 * gscale) (ties to
     the smaller magnitude)."""
     M, K = w.shape
-    Kt = math.ceil(K / BK)
+    Kt = _code_tiles(K)
     Mt = math.ceil(M / BM)
     wf = torch.zeros(M, Kt * BK, dtype=torch.float32, device=w.device)
     wf[:, :K] = w.float()

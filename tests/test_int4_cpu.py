@@ -48,7 +48,7 @@ def test_pack_layout_matches_kernel_emulation(M, K, group):
     torch.manual_seed(M + K)
     w = torch.randn(M, K) * 0.05
     W = int4.quantize(w, group)
-    assert W.qp.shape == (-(-M // 128), -(-K // 64), 128, 32)
+    assert W.qp.shape == (-(-M // 128), 2 * -(-K // 128), 128, 32)
     assert torch.equal(_kernel_emulation(W), W.dequantize())
     # round to nearest: error at most half a step (plus the bf16 rounding)
     q, z, s = W.codes()
