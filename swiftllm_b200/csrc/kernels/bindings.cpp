@@ -65,6 +65,8 @@ void moe_permute(torch::Tensor ids, int64_t e0, int64_t E_local, torch::Tensor o
                  torch::Tensor perm_token, torch::Tensor inv_slot);
 void moe_combine(torch::Tensor out, torch::Tensor y, torch::Tensor weights, torch::Tensor inv_slot);
 void moe_gather(torch::Tensor xg, torch::Tensor x, torch::Tensor perm_token);
+int64_t tp_gather_vocab(std::vector<int64_t> bases, int64_t mc, int64_t rank, torch::Tensor logits,
+                        int64_t dst_off, int64_t ctr_off, torch::Tensor epochs, double timeout_s);
 void spec_verify_greedy(torch::Tensor logits, torch::Tensor pos, torch::Tensor draft,
                         torch::Tensor temp, torch::Tensor out);
 int64_t gemm_w4a16(torch::Tensor out, torch::Tensor x, torch::Tensor qp, torch::Tensor sz,
@@ -120,5 +122,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_w4a16", &swift::gemm_w4a16);
   m.def("gemm_nvfp4w", &swift::gemm_nvfp4w);
   m.def("moe_gather", &swift::moe_gather);
+  m.def("tp_gather_vocab", &swift::tp_gather_vocab);
   m.def("spec_verify_greedy", &swift::spec_verify_greedy);
 }

@@ -406,6 +406,79 @@ int64_t tp_vocab_argmax(std::vector<int64_t> bases, int64_t mc, int64_t rank, to
   return 1;
 }
 
+// ---- vocab-parallel logits all-gather (sampled / logprob steps)
+// Rank j holds the fp32 logits of vocabulary slice [j*Vs, (j+1)*Vs) for
+// every sampled row. Block b pushes rows b, b + grid, ... of this rank's
+// slice into column block j of every rank's [rows, k*Vs] gather buffer (one
+// multimem.st of 16 bytes per 4 logits, or k peer stores), then meets block
+// b of the peers on its counter (arrival after its stores); when every block
+// has passed, each rank holds the full rows locally. The gather buffer is
+// only rewritten after a later step's TP reductions, which order every rank
+// past its readers of this one.
+constexpr int kGaThreads = 256;
+constexpr int kGaBlocks = 64;
+
+template <bool MC>
+__global__ void __launch_bounds__(kGaThreads)
+    tp_gather_vocab_kernel(RnPeers P, int rank, int k, const float* __restrict__ logits,
+                           int64_t ld, int Vs, int rows, int64_t dst_off, int64_t ctr_off,
+                           uint32_t* __restrict__ epochs, int64_t timeout_ns, int* status) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t e = epochs[blockIdx.x];
+  const int V = Vs * k, nv = Vs / 4;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4* src = reinterpret_cast<const float4*>(logits + int64_t(r) * ld);
+    const int64_t byte0 = dst_off + (int64_t(r) * V + int64_t(rank) * Vs) * 4;
+    for (int i = threadIdx.x; i < nv; i += kGaThreads) {
+      const float4 v = src[i];
+      if constexpr (MC) {
+        mc_st_f32x4(P.mc + byte0 + int64_t(i) * 16, v);
+      } else {
+        for (int p = 0; p < k; ++p) {
+          const int q = (rank + p) % k;
+          *reinterpret_cast<float4*>(P.base[q] + byte0 + int64_t(i) * 16) = v;
+        }
+      }
+    }
+  }
+  if (!rn_barrier<MC>(P, rank, k, ctr_off, (e + 1) * uint32_t(k), timeout_ns, status, 240)) return;
+  if (threadIdx.x == 0) epochs[blockIdx.x] = e + 1;
+}
+
+// logits: this rank's fp32 [rows, Vs] slice (row stride may exceed Vs);
+// dst_off: byte offset of the [rows, k*Vs] fp32 gather buffer in the
+// symmetric allocation; ctr_off: kGaBlocks u32 counters; epochs: int32
+// [kGaBlocks] local. Returns the number of kernels launched.
+int64_t tp_gather_vocab(std::vector<int64_t> bases, int64_t mc, int64_t rank, torch::Tensor logits,
+                        int64_t dst_off, int64_t ctr_off, torch::Tensor epochs, double timeout_s) {
+  const RnPeers P = rn_peers(bases, mc);
+  const int k = static_cast<int>(bases.size());
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1);
+  const int rows = static_cast<int>(logits.size(0)), Vs = static_cast<int>(logits.size(1));
+  TORCH_CHECK(Vs % 4 == 0 && logits.stride(0) % 4 == 0 &&
+                  reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0,
+              "tp_gather_vocab: 16-byte rows");
+  TORCH_CHECK(dst_off % 16 == 0 && ctr_off % 4 == 0);
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= kGaBlocks && epochs.is_cuda());
+  if (rows == 0) return 0;
+  const int64_t tns = static_cast<int64_t>(timeout_s * 1e9);
+  auto ep = reinterpret_cast<uint32_t*>(epochs.data_ptr<int32_t>());
+  // every rank computes the same grid from rows, so block b's counter and
+  // epoch advance alike on all ranks
+  const int blocks = std::min(kGaBlocks, rows);
+  if (P.mc)
+    launch_pdl(tp_gather_vocab_kernel<true>, dim3(blocks), dim3(kGaThreads), 0, cur_stream(),
+               P, static_cast<int>(rank), k, logits.data_ptr<float>(), logits.stride(0), Vs, rows,
+               dst_off, ctr_off, ep, tns, status_word_ptr());
+  else
+    launch_pdl(tp_gather_vocab_kernel<false>, dim3(blocks), dim3(kGaThreads), 0, cur_stream(),
+               P, static_cast<int>(rank), k, logits.data_ptr<float>(), logits.stride(0), Vs, rows,
+               dst_off, ctr_off, ep, tns, status_word_ptr());
+  SWIFT_CHECK_LAUNCH();
+  return 1;
+}
+
 // Test hook: one bounded wait on a flag nobody sets (single GPU, no peer):
 // must return with kErrPeerTimeout recorded, the context still usable.
 __global__ void flag_wait_probe_kernel(const uint32_t* flag, uint32_t want, int64_t timeout_ns,

@@ -21,10 +21,12 @@ greedy sampling (``vocab_greedy``) exchanges one (max, argmax, sum-exp)
 candidate per row and rank instead of gathering fp32 logits.
 
 Layout of the symmetric allocation (bytes):
-  [counters 32 KiB | in | out | out2 | cand]
+  [counters 36 KiB | in | out | out2 | cand | gather]
   counters: reduce_norm blocks at 0, plain all-reduce blocks at 1 KiB,
-  vocab rows at 4 KiB (up to 7168 rows); in / out / out2: (max_tokens + 8)
-  x H bf16; cand: k x max_rows float4.
+  vocab rows at 4 KiB (up to 7168 rows), logits-gather blocks at 32 KiB;
+  in / out / out2: (max_tokens + 8) x H bf16; cand: k x max_rows float4;
+  gather: 512 x V fp32 (full-vocabulary logits of sampled / logprob steps,
+  ``gather_vocab``).
 ``SWIFTLLM_MULTIMEM=0`` forces the peer-load path (no multicast object).
 
 Parity: crates/swiftllm-core/src/execution/tensor_parallel.rs (all_reduce /
@@ -46,8 +48,10 @@ from .failures import CommTimeoutError
 
 log = get_logger(__name__)
 
-_CTR_BYTES = 32 << 10
-_CTR_NORM, _CTR_AR, _CTR_VOCAB = 0, 1 << 10, 4 << 10
+_CTR_BYTES = 36 << 10
+_CTR_NORM, _CTR_AR, _CTR_VOCAB, _CTR_GATHER = 0, 1 << 10, 4 << 10, 32 << 10
+_GA_BLOCKS = 64           # kGaBlocks in tp_nvls.cu
+_GATHER_ROWS = 512        # sampled rows the fused logits gather holds (more: NCCL)
 _RN_BLOCKS = 128          # kRnBlocks in tp_nvls.cu
 _MAX_ROWS = 7168          # vocab counters fit the counter region
 TIMEOUT_S = float(os.environ.get("SWIFTLLM_COMM_TIMEOUT", "5.0"))
@@ -71,7 +75,9 @@ class FusedTP(NcclTP):
         self.max_rows = min(_MAX_ROWS, max_tokens)
         self.buf_bytes = ((max_tokens + 8) * H * 2 + 255) // 256 * 256
         self.cand_bytes = (size * self.max_rows * 16 + 255) // 256 * 256
-        total = _CTR_BYTES + 3 * self.buf_bytes + self.cand_bytes
+        self.vocab = model_cfg.vocab_size
+        self.gather_bytes = (_GATHER_ROWS * self.vocab * 4 + 255) // 256 * 256
+        total = _CTR_BYTES + 3 * self.buf_bytes + self.cand_bytes + self.gather_bytes
         self.symm = symm_mem.empty(total // 2, dtype=torch.bfloat16, device=device)
         self.symm.zero_()
         torch.cuda.synchronize(device)
@@ -89,8 +95,10 @@ class FusedTP(NcclTP):
         self.out_off = _CTR_BYTES + self.buf_bytes
         self.out2_off = _CTR_BYTES + 2 * self.buf_bytes
         self.cand_off = _CTR_BYTES + 3 * self.buf_bytes
+        self.gather_off = self.cand_off + self.cand_bytes
         z = lambda n: torch.zeros(n, dtype=torch.int32, device=device)  # noqa: E731
         self.ep_norm, self.ep_ar, self.ep_vocab = z(_RN_BLOCKS), z(_RN_BLOCKS), z(self.max_rows)
+        self.ep_gather = z(_GA_BLOCKS)
         dist.barrier()
         log.info("fused TP comm ready: rank %d/%d, %.1f MiB symmetric, %s", rank, size,
                  total / 2**20, "NVLS multimem" if mc else "peer loads/stores")
@@ -147,6 +155,22 @@ class FusedTP(NcclTP):
         return self.reduce(ops.linear(x, w, b, out=self.reduce_buffer(T, w.shape[0])))
 
     # ------------------------------------------------------------ sampling
+    def gather_vocab(self, x: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary fp32 logits [rows, V] from every rank's slice
+        [rows, V/k]: one kernel pushes this rank's slice into every rank's
+        gather buffer over NVSwitch (multimem.st) or NVLink peer stores."""
+        rows = x.shape[0]
+        if (x.dtype != torch.float32 or rows > _GATHER_ROWS or x.shape[-1] * self.size != self.vocab
+                or x.shape[-1] % 4):
+            return super().gather_vocab(x)
+        from .. import ops
+        x = x.contiguous()
+        ops._count(self.C.tp_gather_vocab(self.bases, self.mc, self.rank, x, self.gather_off,
+                                          _CTR_GATHER, self.ep_gather, TIMEOUT_S))
+        n = rows * self.vocab
+        return self.symm[self.gather_off // 2:self.gather_off // 2 + 2 * n].view(torch.float32).view(
+            rows, self.vocab)
+
     def vocab_greedy(self, logits: torch.Tensor, v0: int) -> Tuple[torch.Tensor, torch.Tensor]:
         """Greedy tokens and their log-probabilities over the full vocabulary
         from this rank's fp32 logits slice [rows, V/k] starting at ``v0``;

@@ -87,6 +87,13 @@ def main():
             assert torch.equal(tok.long(), want), (tok[:4], want[:4])
             ref_lp = torch.log_softmax(full, -1).gather(1, want.view(-1, 1)).view(-1)
             torch.testing.assert_close(lp, ref_lp, rtol=1e-3, atol=1e-3)
+            # fused all-gather of vocab-parallel fp32 logits: bit-identical to
+            # NCCL's all_gather (twice, so a stale buffer would show)
+            for _ in range(2):
+                lv = torch.randn(T, cfg.vocab_size // world, device=dev, generator=g)
+                lvs = [torch.empty_like(lv) for _ in range(world)]
+                dist.all_gather(lvs, lv)
+                assert torch.equal(tp.gather_vocab(lv), torch.cat(lvs, dim=-1))
         st = tp.C.read_status(True)
         assert st[0] == 0, st
     m = DecoderModel(cfg, dtype, dev, tp)
