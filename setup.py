@@ -42,8 +42,6 @@ def cuda_ext():
             "-gencode", "arch=compute_100a,code=sm_100a",
             "-U__CUDA_NO_HALF_OPERATORS__", "-U__CUDA_NO_HALF_CONVERSIONS__",
             "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_HALF2_OPERATORS__"]
-    if os.environ.get("SWIFT_CHECKS") == "1":
-        nvcc.append("-DSWIFT_CHECKS=1")
     if os.environ.get("SWIFTLLM_PTXAS_V") == "1":
         nvcc.append("-Xptxas=-v")
     return CUDAExtension(

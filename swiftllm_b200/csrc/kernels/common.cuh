@@ -27,9 +27,10 @@
 
 namespace swift {
 
-// Device status word: kernels that give up a bounded wait (or, in
-// SWIFT_CHECKS builds, detect an out-of-range index) record a code here and
-// return instead of trapping. The host reads and clears it.
+// Device status word: kernels that give up a bounded wait, or whose
+// always-on index guards find an out-of-range index, record a code here and
+// return (or skip the access) instead of trapping. The host reads and clears
+// it.
 enum StatusCode : int {
   kOk = 0,
   kErrWaitTimeout = 1,
