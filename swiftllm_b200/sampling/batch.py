@@ -25,20 +25,14 @@ def row_keys(seed: np.ndarray, step_idx: np.ndarray, engine_seed: int,
              step: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
     """(key uint64, c0 uint32, c1 uint32) per row."""
     n = seed.shape[0]
-    keys = np.empty(n, dtype=np.uint64)
-    c0 = np.empty(n, dtype=np.uint32)
-    c1 = np.empty(n, dtype=np.uint32)
+    seed = np.asarray(seed, dtype=np.int64)
     seeded = seed >= 0
-    ekey = mix_key(engine_seed, 0xA11)
-    for i in range(n):
-        if seeded[i]:
-            keys[i] = mix_key(int(seed[i]), 0x5EED)
-            c0[i] = int(step_idx[i]) & 0xFFFFFFFF
-            c1[i] = 0
-        else:
-            keys[i] = ekey
-            c0[i] = step & 0xFFFFFFFF
-            c1[i] = i
+    # mix_key(seed, 0x5EED) for seeded rows, vectorised: (seed << 32) | tid
+    sk = ((seed.astype(np.uint64) & np.uint64(0xFFFFFFFF)) << np.uint64(32)) | np.uint64(0x5EED)
+    keys = np.where(seeded, sk, np.uint64(mix_key(engine_seed, 0xA11))).astype(np.uint64)
+    c0 = np.where(seeded, np.asarray(step_idx, dtype=np.int64) & 0xFFFFFFFF,
+                  step & 0xFFFFFFFF).astype(np.uint32)
+    c1 = np.where(seeded, 0, np.arange(n)).astype(np.uint32)
     return keys, c0, c1
 
 

@@ -355,3 +355,19 @@ def test_kv_bytes():
     c = ModelConfig(num_layers=1, num_kv_heads=8, head_dim=128)
     assert c.kv_cache_bytes_per_token(2) == 4096  # K + V: 2 x 8 x 128 x 2 B
     assert 16 * c.kv_cache_bytes_per_token(2) == 65536
+
+
+def test_row_keys_vectorised_matches_mix_key():
+    # per-row Philox keys / counters: seeded rows use (seed, step index),
+    # the others the engine key with (step, row)
+    import numpy as np
+    from swiftllm_b200.parallel.dummy_init import mix_key
+    from swiftllm_b200.sampling.batch import row_keys
+    seed = np.array([-1, 5, 2 ** 40 + 3, -1, 0])
+    si = np.array([3, 7, 9, 2 ** 33 + 1, 0])
+    k, c0, c1 = row_keys(seed, si, 1234, 77)
+    for i in range(5):
+        if seed[i] >= 0:
+            assert (k[i], c0[i], c1[i]) == (mix_key(int(seed[i]), 0x5EED), int(si[i]) & 0xFFFFFFFF, 0)
+        else:
+            assert (k[i], c0[i], c1[i]) == (mix_key(1234, 0xA11), 77, i)
