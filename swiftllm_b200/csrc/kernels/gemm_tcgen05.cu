@@ -1157,6 +1157,8 @@ static void plan(int M, int N, int K, int* bn, int* splits) {
   int k_iters = (K + kGemmBK - 1) / kGemmBK;
   int s = 1;
   if (tiles < sms * 3 / 4) s = std::max(1, std::min({(sms + tiles - 1) / tiles, k_iters / 4, 8}));
+  // only as many splits as non-empty K ranges of ceil(k_iters / s) steps
+  if (s > 1) s = (k_iters + (k_iters + s - 1) / s - 1) / ((k_iters + s - 1) / s);
   *bn = b;
   *splits = s;
 }

@@ -605,6 +605,13 @@ static int64_t gemm_w4_impl(torch::Tensor out, torch::Tensor x, torch::Tensor qp
   int splits = 1;
   if (tiles < sms * 3 / 4)
     splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({(sms + tiles - 1) / tiles, Kt / 8, 8})));
+  {  // only as many splits as non-empty K ranges (the kernel gives each
+     // split ceil(k_iters / splits) steps; a split past the end would publish
+     // an accumulator it never wrote)
+    const int k_iters = static_cast<int>(Kt / w4::KSUB);
+    const int k_per = (k_iters + splits - 1) / splits;
+    splits = (k_iters + k_per - 1) / k_per;
+  }
   CUtensorMap tx = make_tmap_2d(x.data_ptr(), T, K, ldx, w4::BK, bn);
   auto y = reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>());
   const __nv_bfloat16* bp =

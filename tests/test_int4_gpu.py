@@ -18,7 +18,8 @@ def C():
 # several token tiles; M covers a partial feature tile; K a partial k step.
 @pytest.mark.parametrize("T,M,K,group", [(1, 4096, 4096, 128), (37, 200, 328, 64),
                                          (256, 12288, 4096, 128), (5, 4096, 11008, 128),
-                                         (300, 1000, 1024, 128), (1000, 512, 2048, 256)])
+                                         (300, 1000, 1024, 128), (1000, 512, 2048, 256),
+                                         (1, 1024, 4224, 128)])  # 33 k steps over split-K
 def test_gemm_w4a16(C, T, M, K, group):
     from swiftllm_b200.ops import int4
     torch.manual_seed(T + M + K)
